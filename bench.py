@@ -1,0 +1,467 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a attention forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (fp16 q, k, v of layout [B*H, N, 64], non-causal, scale 1/8):
+  b1h8n8192     B=1  H=8  N=8192   N(0,1)            the headline configuration (default)
+  b16h16n4096   B=16 H=16 N=4096   N(0,1)            throughput shape
+  b1h32n32768   B=1  H=32 N=32768  q,k ~ N(0,3^2)    long sequence, peaky softmax
+  b128h16n512   B=128 H=16 N=512   uniform[-1,1]     short sequence, HBM side of the ridge
+
+Method (as benchs/benchmark_forward.py:218-325 of the reference): 4 rotating input buffers
+seeded 0..3 (q, k, v drawn in that order from one generator per buffer), a 256 MB L2 flush
+write before every step (outside the timed interval), CUDA events on the launching stream
+around each forward call, TFLOPS = 4*B*H*N^2*D / t. W warm-up steps, then exactly K timed
+steps bracketed by barrier + synchronize; the time is the max over ranks.
+
+Multi-GPU (torchrun, one rank per GPU): every rank owns a contiguous block of batch*head rows
+(mini_flash_attention.sharding); no collective runs on the data path. For the headline
+workload each rank owns its own B=1, H=8 slice (weak scaling: the global batch grows with N);
+for the others the global B*H is split over the ranks (strong scaling).
+
+--impl reference times the reference's CPU path (the naive torch attention of
+benchs/benchmark_forward.py:98-115) on this host's cores, one head of the workload per step,
+on rank 0 only; --impl reference --ref-kernel cute times the reference's own CuTe kernel
+(built from its sources into oracle/_ref) on the GPU instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "mini-flash-attention_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "fwd TFLOPS/GPU (4·BH·N²·D/t), % dense-fp16 peak; ms at B1 H8 N8192"
+UNIT = "TFLOPS"
+PUBLISHED_TFLOPS = 9.510  # ms, RTX A4000, CuTe kernel at B1 H8 N8192 (reference README.md:97)
+PUBLISHED_TFLOPS = 4 * 8 * 8192 ** 2 * 64 / (PUBLISHED_TFLOPS * 1e-3) / 1e12
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+L2_FLUSH_MB = 256
+INPUT_BUFFERS = 4
+
+WORKLOADS = {
+    "b1h8n8192": dict(B=1, H=8, N=8192, dist="normal", qk_scale=1.0, scaling="weak"),
+    "b16h16n4096": dict(B=16, H=16, N=4096, dist="normal", qk_scale=1.0, scaling="strong"),
+    "b1h32n32768": dict(B=1, H=32, N=32768, dist="normal", qk_scale=3.0, scaling="strong"),
+    "b128h16n512": dict(B=128, H=16, N=512, dist="uniform", qk_scale=1.0, scaling="strong"),
+}
+D = 64
+
+
+def attention_flops(bh: int, n: int, d: int = D) -> float:
+    return 4.0 * bh * n * n * d
+
+
+def attention_bytes(bh: int, n: int, d: int = D) -> float:
+    return 4.0 * bh * n * d * 2  # read q, k, v once, write o once (fp16)
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except (OSError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(kernel: str, workload: str) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    path = ROOT / "profiles" / f"{kernel}_{workload}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------- clocks during timing
+REASON_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons of one GPU every few ms (NVML, else
+    nvidia-smi) while the timed region runs."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.device_index = device_index
+        self.period = period_s
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._proc = None
+
+    def start(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = self.device_index
+            if visible:
+                ids = [x for x in visible.split(",") if x.strip()]
+                if idx < len(ids) and ids[idx].strip().isdigit():
+                    idx = int(ids[idx])
+            h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._nvml = (pynvml, h)
+            self._thread = threading.Thread(target=self._run_nvml, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001
+            self._nvml = None
+        return self
+
+    def _run_nvml(self):
+        pynvml, h = self._nvml
+        get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                reasons = int(get_reasons(h))
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        mhz = statistics.median(s[0] for s in busy)
+        seen = 0
+        for _, r in busy:
+            seen |= r
+        reasons = [name for bit, name in REASON_BITS.items() if seen & bit and bit != 0x1]
+        return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(busy)}
+
+
+# ---------------------------------------------------------------- inputs
+def make_inputs(wl: dict, bh: int, seed: int, device) -> tuple:
+    """One buffer: q, k, v drawn in that order from one generator (benchmark_forward.py:222-227)."""
+    shape = (bh, wl["N"], D)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    if wl["dist"] == "uniform":
+        q, k, v = (torch.rand(shape, device=device, generator=g, dtype=torch.float32) * 2 - 1
+                   for _ in range(3))
+    else:
+        q, k, v = (torch.randn(shape, device=device, generator=g, dtype=torch.float32)
+                   for _ in range(3))
+        q, k = q * wl["qk_scale"], k * wl["qk_scale"]
+    return q.half().contiguous(), k.half().contiguous(), v.half().contiguous()
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
+    """The reference's naive torch attention on the host cores, one head of the workload."""
+    from oracle.torch_naive import torch_naive_attention
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v = make_inputs(wl, 1, 0, "cpu")
+    flops = attention_flops(1, wl["N"])
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while True:
+        t0 = time.perf_counter()
+        torch_naive_attention(q, k, v)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(times) >= 50:
+            break
+    t = statistics.median(times)
+    return {"value": flops / t / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"1 of {wl['B'] * wl['H']} heads ([1,{wl['N']},64]), naive fp32 torch "
+                      f"attention (benchs/benchmark_forward.py:98-115), median of {len(times)} "
+                      f"runs in {sum(times):.1f} s"}
+
+
+# ---------------------------------------------------------------- arms
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_ours(args, wl) -> dict | None:
+    import mini_flash_attention as mfa
+    from mini_flash_attention.sharding import bh_shard
+
+    rank, world, local = init_dist()
+    dev = torch.device("cuda", local)
+    if wl["scaling"] == "weak":
+        global_bh = wl["B"] * wl["H"] * world
+        shard = bh_shard(global_bh, rank, world)
+    else:
+        global_bh = wl["B"] * wl["H"]
+        shard = bh_shard(global_bh, rank, world)
+    bh = shard.rows
+    n = wl["N"]
+    inputs = [make_inputs(wl, bh, rank * INPUT_BUFFERS + i, dev) for i in range(INPUT_BUFFERS)]
+    flush = torch.empty(L2_FLUSH_MB * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    fwd = mfa.forward
+    stream = torch.cuda.current_stream(dev)
+
+    with torch.inference_mode():
+        for i in range(args.warmup):
+            flush.fill_(1.0)
+            fwd(*inputs[i % INPUT_BUFFERS])
+        torch.cuda.synchronize(dev)
+
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        sampler = ClockSampler(local).start()
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        wall0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(1.0)  # L2 flush, outside the event interval
+            starts[i].record(stream)
+            fwd(*inputs[i % INPUT_BUFFERS])
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        wall = time.perf_counter() - wall0
+        clocks = sampler.stop()
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        total_ms = max_over_ranks(sum(step_ms), world)
+
+        # ---- end to end: pinned host inputs -> device -> forward -> host output
+        host_in = [x.cpu().pin_memory() for x in inputs[0]]
+        dev_in = [torch.empty_like(x) for x in inputs[0]]
+        host_out = torch.empty(inputs[0][0].shape, dtype=torch.float16).pin_memory()
+        e2e_steps = max(args.steps, 3)
+        for _ in range(2):
+            for h, d_ in zip(host_in, dev_in):
+                d_.copy_(h, non_blocking=True)
+            host_out.copy_(fwd(*dev_in), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            for h, d_ in zip(host_in, dev_in):
+                d_.copy_(h, non_blocking=True)
+            host_out.copy_(fwd(*dev_in), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+        barrier(world)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+
+    flops_rank_step = attention_flops(bh, n)
+    job_flops_step = attention_flops(global_bh, n)
+    value = job_flops_step * args.steps / (total_ms / 1e3) / 1e12
+    kernel_ms = total_ms / args.steps
+    achieved = flops_rank_step / (kernel_ms / 1e3) / 1e12
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    traffic = load_traffic("mfa_fwd", args.workload)
+    e2e_value = job_flops_step * e2e_steps / (e2e_ms / 1e3) / 1e12
+    bytes_in = 3 * global_bh * n * D * 2
+    bytes_out = global_bh * n * D * 2
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(kernel_ms, 4),
+        "higher_is_better": True,
+        "scaling": wl["scaling"],
+        "vs_baseline": round(value / PUBLISHED_TFLOPS, 2),
+        "dtype": "fp16",
+        "data": "synthetic (seeded, shapes and distributions of the workload; no dataset)",
+        "config": {
+            "workload": args.workload,
+            "B": wl["B"] * (world if wl["scaling"] == "weak" else 1), "H": wl["H"], "N": n,
+            "D": D, "bh_per_gpu": bh, "causal": False,
+            "parallelism": f"batch*head sharded over {world} GPU(s), no collective",
+            "l2": f"{L2_FLUSH_MB} MB write before every step, outside the timed interval",
+            "input_buffers": INPUT_BUFFERS,
+            "timing": "CUDA events around each forward() call on its stream, max over ranks",
+        },
+        "tflops_per_gpu": round(value / world, 3),
+        "pct_dense_fp16_peak": round(100.0 * achieved / peak, 2),
+        "roofline": {
+            "bound": "tensor",
+            "achieved": round(achieved, 3),
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": traffic,
+            "algorithmic_bytes": attention_bytes(bh, n),
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops burst)"
+            if peak_src == "measured" else "fallback 1.59 PFLOP/s",
+            "kernel": "mfa_fwd_kernel<2,3>",
+        },
+        "e2e": {
+            "value": round(e2e_value, 3), "unit": UNIT,
+            "h2d_bytes_per_step": bytes_in, "d2h_bytes_per_step": bytes_out,
+            "path": "pinned host q,k,v -> cudaMemcpyAsync -> mini_flash_attention.forward -> "
+                    "pinned host out, one stream",
+        },
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "wall_s_timed_region": round(wall, 4),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(wl)
+    return line
+
+
+def run_reference(args, wl) -> dict | None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    if args.ref_kernel == "cute":
+        return run_reference_cute(args, wl)
+    from oracle.torch_naive import torch_naive_attention
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v = make_inputs(wl, 1, 0, "cpu")
+    for _ in range(args.warmup):
+        torch_naive_attention(q, k, v)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        torch_naive_attention(q, k, v)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = attention_flops(1, wl["N"]) * args.steps / total / 1e12
+    sample = (f"1 of {wl['B'] * wl['H']} heads ([1,{wl['N']},64]) per step, naive fp32 torch "
+              f"attention (benchs/benchmark_forward.py:98-115) on {threads} host threads")
+    return {
+        "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic (seeded)", "impl": "reference",
+        "config": {"workload": args.workload, "B": wl["B"], "H": wl["H"], "N": wl["N"], "D": D,
+                   "sample": "one head per step"},
+        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_reference_cute(args, wl) -> dict:
+    """The reference's own CuTe kernel (oracle/_ref, built from its sources) on this GPU."""
+    from oracle import ref
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    bh, n = wl["B"] * wl["H"], wl["N"]
+    inputs = [make_inputs(wl, bh, i, dev) for i in range(INPUT_BUFFERS)]
+    flush = torch.empty(L2_FLUSH_MB * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        flush.fill_(1.0)
+        ref.reference_forward(*inputs[i % INPUT_BUFFERS])
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(1.0)
+        starts[i].record(stream)
+        ref.reference_forward(*inputs[i % INPUT_BUFFERS])
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total = sum(ms)
+    value = attention_flops(bh, n) * args.steps / (total / 1e3) / 1e12
+    return {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps, 4),
+            "median_ms": round(statistics.median(ms), 4), "higher_is_better": True,
+            "scaling": wl["scaling"], "vs_baseline": round(value / PUBLISHED_TFLOPS, 2),
+            "dtype": "fp16", "data": "synthetic (seeded)", "impl": "reference",
+            "ref_kernel": "FlashAttnCuteKernel (src/mini_flash_attention/flash_attn_cuda.cu), "
+                          "built for sm_100a from the reference sources, zeros_like output "
+                          "inside the timed call as in the reference binding",
+            "config": {"workload": args.workload, "B": wl["B"], "H": wl["H"], "N": n, "D": D}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="b1h8n8192")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ref-kernel", choices=["cpu", "cute"], default="cpu")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    wl = WORKLOADS[args.workload]
+    line = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,93 @@
+/*
+ * mini-flash-attention for B200 (sm_100a) -- C ABI of the attention forward.
+ *
+ * Plain pointers and sizes only; no torch or C++ types cross this boundary, and no call
+ * throws. Every entry point returns MFA_OK (0) or an MFA_ERR_* code; the message of the last
+ * failure on the calling thread is available from mfa_last_error_string().
+ *
+ * Tensor contract (identical to the reference binding, src/mini_flash_attention/flash_attn.cpp:
+ * 45-109): q, k, v and out are device pointers to contiguous fp16 arrays laid out [BH, N, D]
+ * (BH = batch * heads), D = 64, out is written completely by the kernel. Launches are
+ * asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream) and on the device
+ * that is current for the calling thread, exactly like the reference launchers.
+ */
+#ifndef MFA_B200_H
+#define MFA_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MFA_API __attribute__((visibility("default")))
+#else
+#define MFA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mfa_status_code {
+  MFA_OK = 0,
+  MFA_ERR_INVALID_ARGUMENT = 1, /* null / misaligned pointer, negative or oversized extent */
+  MFA_ERR_HEAD_DIM = 2,         /* D != 64 */
+  MFA_ERR_SEQ_LEN = 3,          /* N not a multiple of the entry point's block size */
+  MFA_ERR_CAUSAL = 4,           /* causal masking requested from an entry point without it */
+  MFA_ERR_CUDA = 5,             /* CUDA runtime or driver error; message has the details */
+  MFA_ERR_DEVICE = 6            /* current device is not an sm_100 (B200-class) GPU */
+};
+
+/*
+ * Attention forward, tcgen05 kernel with two query tiles (256 rows) per CTA.
+ * Replaces the reference launcher launch_flash_attn_forward
+ * (src/mini_flash_attention/flash_attn_cuda.cu:370-420): same arguments, same checks in the
+ * same order (D == 64, N % 128 == 0, causal == 0) with the same messages. `scale` multiplies
+ * q.k before the softmax (the reference binding passes 1/sqrt(D), flash_attn.cpp:94).
+ * bh == 0 or n == 0 is a no-op that returns MFA_OK.
+ */
+MFA_API int mfa_fwd_f16(const void* q, const void* k, const void* v, void* out, int64_t bh, int64_t n,
+                int32_t d, float scale, int32_t causal, void* stream);
+
+/*
+ * Attention forward, single-query-tile tcgen05 kernel (128 rows per CTA, 2-stage K/V ring).
+ * Replaces the reference's WMMA launcher, declared as launch_flash_attn_forward_wmma
+ * (src/mini_flash_attention/flash_attn.cpp:21-31) and implemented at
+ * src/mini_flash_attention/flash_attn_wmma_cuda.cu:253-289: checks D == 64, N % 64 == 0,
+ * causal == 0 with that launcher's messages.
+ */
+MFA_API int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, void* out, int64_t bh,
+                       int64_t n, int32_t d, float scale, int32_t causal, void* stream);
+
+/* Message of the last failing call made by this thread ("" if none). Replaces the
+ * std::runtime_error text of the reference launchers and check_cuda
+ * (src/mini_flash_attention/utils.cuh:15-21). */
+MFA_API const char* mfa_last_error_string(void);
+
+/*
+ * Reads the device-side status word of `device` (synchronises that device first).
+ * 0 = every kernel finished normally; 0x100 + site = a bounded mbarrier wait in some CTA
+ * expired and that CTA unwound without writing its output tile. If `reset` is non-zero the
+ * word is cleared afterwards. No reference counterpart: the reference kernels have no
+ * bounded waits.
+ */
+MFA_API int mfa_device_status(int device, int* status, int reset);
+
+/* Per-wait watchdog limit in nanoseconds used by later launches (default 2 s, min 1 ms).
+ * No reference counterpart. */
+MFA_API int mfa_set_watchdog_ns(uint64_t ns);
+
+/*
+ * Self-test of the watchdog path: launches a one-CTA kernel on `stream` that allocates TMEM,
+ * waits on an mbarrier that nothing arrives at with the given limit, records the expiry in
+ * its own status word, frees TMEM and returns. *status_out receives that word (0x100 + site
+ * when the wait expired as designed). Synchronises `stream`. No reference counterpart.
+ */
+MFA_API int mfa_watchdog_selftest(void* stream, uint64_t timeout_ns, int* status_out);
+
+/* Library version string. */
+MFA_API const char* mfa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MFA_B200_H */

@@ -1,0 +1,282 @@
+// C-ABI launchers of the sm_100a attention forward (declared in include/mfa_b200.h).
+//
+// Host-side duties of the reference launchers (src/mini_flash_attention/flash_attn_cuda.cu:
+// 370-420 and flash_attn_wmma_cuda.cu:253-289): validate D / N / causal with the same
+// messages, build the grid, launch on the caller's stream, report launch errors. On top of
+// that this layer encodes the four TMA tensor maps and converts every failure into a status
+// code plus a thread-local message instead of a C++ exception.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/mfa_b200.h"
+#include "mfa_fwd_kernel.cuh"
+
+namespace mfa {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr const char* kVersion = "mini-flash-attention-b200 0.1.0 (sm_100a)";
+
+thread_local std::string g_last_error;
+
+// Device status word written by the watchdog of every forward kernel in this library.
+__device__ int g_device_status = 0;
+
+unsigned long long g_watchdog_ns = 2000000000ull;  // 2 s per wait
+
+using FullKernel = FwdConfig<2, 3>;
+using SimpleKernel = FwdConfig<1, 2>;
+
+struct DeviceState {
+  std::once_flag once;
+  int error = MFA_OK;
+  std::string message;
+  int* status_ptr = nullptr;
+};
+DeviceState g_devices[kMaxDevices];
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int fail_cuda(cudaError_t e, const char* what) {
+  return fail(MFA_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(e) + " (" + what + ")");
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(std::string* why) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  static std::string err;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    cudaError_t e =
+        cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || ptr == nullptr) {
+      err = std::string("cannot resolve cuTensorMapEncodeTiled: ") + cudaGetErrorString(e);
+      return;
+    }
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn && why) *why = err;
+  return fn;
+}
+
+// One-time per-device set-up: architecture check, kernel attributes, status word address.
+int prepare_device(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(MFA_ERR_DEVICE, "device index out of range");
+  DeviceState& ds = g_devices[dev];
+  std::call_once(ds.once, [&ds, dev] {
+    int major = 0, minor = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) {
+      ds.error = MFA_ERR_CUDA;
+      ds.message = std::string("CUDA error: ") + cudaGetErrorString(e);
+      return;
+    }
+    if (major != 10 || minor != 0) {
+      ds.error = MFA_ERR_DEVICE;
+      ds.message = "mini_flash_attention_b200 kernels are built for sm_100a only; device " +
+                   std::to_string(dev) + " is sm_" + std::to_string(major) + std::to_string(minor);
+      return;
+    }
+    e = cudaFuncSetAttribute(mfa_fwd_kernel<FullKernel::NQ, FullKernel::STAGES>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, FullKernel::kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(mfa_fwd_kernel<SimpleKernel::NQ, SimpleKernel::STAGES>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SimpleKernel::kSmemBytes);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status_ptr), g_device_status);
+    if (e != cudaSuccess) {
+      ds.error = MFA_ERR_CUDA;
+      ds.message = std::string("CUDA error: ") + cudaGetErrorString(e) + " (device set-up)";
+    }
+  });
+  if (ds.error != MFA_OK) return fail(ds.error, ds.message);
+  return MFA_OK;
+}
+
+int encode_bhnd(CUtensorMap* map, const void* base, int64_t n, int64_t bh) {
+  std::string why;
+  auto encode = tensor_map_encoder(&why);
+  if (!encode) return fail(MFA_ERR_CUDA, why);
+  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(bh)};
+  const cuuint64_t strides[2] = {64 * 2, static_cast<cuuint64_t>(n) * 64 * 2};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
+                      strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MFA_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
+  return MFA_OK;
+}
+
+template <class Cfg>
+int launch_forward(const void* q, const void* k, const void* v, void* out, int64_t bh, int64_t n,
+                   float scale, cudaStream_t stream) {
+  if (bh == 0 || n == 0) return MFA_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  int rc = prepare_device(dev);
+  if (rc != MFA_OK) return rc;
+
+  FwdParams p;
+  if ((rc = encode_bhnd(&p.tm_q, q, n, bh)) != MFA_OK) return rc;
+  if ((rc = encode_bhnd(&p.tm_k, k, n, bh)) != MFA_OK) return rc;
+  if ((rc = encode_bhnd(&p.tm_v, v, n, bh)) != MFA_OK) return rc;
+  if ((rc = encode_bhnd(&p.tm_o, out, n, bh)) != MFA_OK) return rc;
+  const int64_t rows_per_cta = static_cast<int64_t>(Cfg::kRows) * Cfg::NQ;
+  const int64_t q_blocks = (n + rows_per_cta - 1) / rows_per_cta;
+  p.n = static_cast<int>(n);
+  p.bh = static_cast<int>(bh);
+  p.q_blocks = static_cast<int>(q_blocks);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.timeout_ns = g_watchdog_ns;
+  p.status = g_devices[dev].status_ptr;
+
+  const int64_t grid = q_blocks * bh;
+  if (grid > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES>
+      <<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
+  return MFA_OK;
+}
+
+int check_common(const void* q, const void* k, const void* v, void* out, int64_t bh, int64_t n,
+                 int32_t d) {
+  if (bh < 0 || n < 0 || d <= 0) return fail(MFA_ERR_INVALID_ARGUMENT, "negative extent");
+  if (bh > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H is too large");
+  if (n > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "N is too large");
+  if (bh == 0 || n == 0) return MFA_OK;
+  if (!q || !k || !v || !out) return fail(MFA_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  const uintptr_t any = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
+  if (any & 15u)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "q, k, v and out must be 16-byte aligned");
+  return MFA_OK;
+}
+
+// ------------------------------------------------------------------ watchdog self-test
+__device__ int g_selftest_status = 0;
+
+__global__ void __launch_bounds__(32, 1) watchdog_selftest_kernel(unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar_storage;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const uint32_t bar = smem_addr(&bar_storage);
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(bar, 1);
+    mbar_init_fence();
+  }
+  tmem_alloc(smem_addr(&tmem_slot), 32);
+  tmem_relinquish();
+  tc_fence_before();
+  __syncwarp();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const Watchdog wd{&abort_flag, &g_selftest_status, timeout_ns};
+  // Nothing ever arrives on `bar`: the wait must expire, trip the watchdog and return.
+  const bool ok = wait_warp(bar, 0, wd, kSiteSoftSFull);
+  (void)ok;
+  tc_fence_before();
+  __syncwarp();
+  tmem_dealloc(tmem, 32);
+}
+
+}  // namespace
+}  // namespace mfa
+
+using namespace mfa;
+
+extern "C" int mfa_fwd_f16(const void* q, const void* k, const void* v, void* out, int64_t bh,
+                           int64_t n, int32_t d, float scale, int32_t causal, void* stream) {
+  int rc = check_common(q, k, v, out, bh, n, d);
+  if (rc != MFA_OK) return rc;
+  // Same checks and messages, in the same order, as flash_attn_cuda.cu:399-410.
+  if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
+  if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
+  if (causal) return fail(MFA_ERR_CAUSAL, "Causal attention is not supported yet");
+  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  return launch_forward<FullKernel>(q, k, v, out, bh, n, scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, void* out,
+                                  int64_t bh, int64_t n, int32_t d, float scale, int32_t causal,
+                                  void* stream) {
+  int rc = check_common(q, k, v, out, bh, n, d);
+  if (rc != MFA_OK) return rc;
+  // Same checks and messages, in the same order, as flash_attn_wmma_cuda.cu:269-277.
+  if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This WMMA prototype supports only D=64 yet");
+  if (n % 64 != 0)
+    return fail(MFA_ERR_SEQ_LEN, "Only N (seq len) divisible by 64 and 64 are supported yet");
+  if (causal) return fail(MFA_ERR_CAUSAL, "Causal attention is not yet supported");
+  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  return launch_forward<SimpleKernel>(q, k, v, out, bh, n, scale,
+                                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" const char* mfa_last_error_string(void) { return g_last_error.c_str(); }
+
+extern "C" int mfa_device_status(int device, int* status, int reset) {
+  if (!status) return fail(MFA_ERR_INVALID_ARGUMENT, "status must not be null");
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return fail_cuda(e, "cudaSetDevice");
+  int rc = prepare_device(device);
+  if (rc == MFA_OK) {
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(status, g_device_status, sizeof(int));
+    if (e == cudaSuccess && reset) {
+      const int zero = 0;
+      e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+    }
+    if (e != cudaSuccess) rc = fail_cuda(e, "reading the device status word");
+  }
+  cudaSetDevice(prev);
+  return rc;
+}
+
+extern "C" int mfa_set_watchdog_ns(uint64_t ns) {
+  if (ns < 1000000ull) return fail(MFA_ERR_INVALID_ARGUMENT, "watchdog limit must be >= 1 ms");
+  g_watchdog_ns = ns;
+  return MFA_OK;
+}
+
+extern "C" int mfa_watchdog_selftest(void* stream, uint64_t timeout_ns, int* status_out) {
+  if (!status_out) return fail(MFA_ERR_INVALID_ARGUMENT, "status_out must not be null");
+  if (timeout_ns < 1000000ull || timeout_ns > 10000000000ull)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "self-test limit must be within [1 ms, 10 s]");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  int rc = prepare_device(dev);
+  if (rc != MFA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int zero = 0;
+  e = cudaMemcpyToSymbolAsync(g_selftest_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return fail_cuda(e, "clearing the self-test status");
+  watchdog_selftest_kernel<<<1, 32, 0, s>>>(timeout_ns);
+  if ((e = cudaGetLastError()) != cudaSuccess) return fail_cuda(e, "self-test launch");
+  e = cudaMemcpyFromSymbolAsync(status_out, g_selftest_status, sizeof(int), 0,
+                                cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail_cuda(e, "self-test");
+  return MFA_OK;
+}
+
+extern "C" const char* mfa_version(void) { return kVersion; }

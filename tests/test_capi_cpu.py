@@ -1,0 +1,119 @@
+"""CPU tests of the C ABI: libmfa_b200.so loads, exports every symbol include/mfa_b200.h
+declares, and rejects bad arguments with the reference launchers' messages before touching
+the GPU (flash_attn_cuda.cu:399-410, flash_attn_wmma_cuda.cu:269-277)."""
+from __future__ import annotations
+
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from mini_flash_attention import capi
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "mfa_b200.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"MFA_API\s+[\w\s\*]+?\b(mfa_\w+)\s*\(", text)
+
+
+def test_header_and_python_view_agree():
+    assert sorted(declared_symbols()) == sorted(capi.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    for sym in declared_symbols():
+        assert sym in exported, sym
+    lib = capi.load()
+    for sym in declared_symbols():
+        assert hasattr(lib, sym)
+
+
+def test_build_targets_only_sm100a():
+    from mini_flash_attention import _build
+
+    assert _build.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_version():
+    assert "sm_100a" in capi.version()
+
+
+FAKE = 0x10000  # never dereferenced: every case below fails validation first
+
+
+@pytest.mark.parametrize("simple", [False, True])
+def test_head_dim_rejected(simple):
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE, FAKE, FAKE, FAKE, 2, 128, 32, 0.17, simple=simple)
+    assert e.value.code == capi.MFA_ERR_HEAD_DIM
+    want = ("This WMMA prototype supports only D=64 yet" if simple
+            else "This kernel supports only D=64")
+    assert str(e.value) == want
+
+
+def test_seq_len_rejected_full_kernel():
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE, FAKE, FAKE, FAKE, 2, 192, 64, 0.125)
+    assert e.value.code == capi.MFA_ERR_SEQ_LEN
+    assert str(e.value) == "Only N divisible by 128 and 128 is supported"
+
+
+def test_seq_len_rejected_simple_kernel():
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE, FAKE, FAKE, FAKE, 2, 96, 64, 0.125, simple=True)
+    assert e.value.code == capi.MFA_ERR_SEQ_LEN
+    assert str(e.value) == "Only N (seq len) divisible by 64 and 64 are supported yet"
+
+
+@pytest.mark.parametrize("simple", [False, True])
+def test_causal_rejected(simple):
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE, FAKE, FAKE, FAKE, 2, 128, 64, 0.125, causal=True, simple=simple)
+    assert e.value.code == capi.MFA_ERR_CAUSAL
+    want = ("Causal attention is not yet supported" if simple
+            else "Causal attention is not supported yet")
+    assert str(e.value) == want
+
+
+def test_check_order_matches_reference():
+    # D is checked before N, N before causal (flash_attn_cuda.cu:399-410)
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE, FAKE, FAKE, FAKE, 1, 100, 32, 0.1, causal=True)
+    assert e.value.code == capi.MFA_ERR_HEAD_DIM
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE, FAKE, FAKE, FAKE, 1, 100, 64, 0.1, causal=True)
+    assert e.value.code == capi.MFA_ERR_SEQ_LEN
+
+
+def test_null_and_misaligned_pointers_rejected():
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(0, FAKE, FAKE, FAKE, 1, 128, 64, 0.125)
+    assert e.value.code == capi.MFA_ERR_INVALID_ARGUMENT
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE + 2, FAKE, FAKE, FAKE, 1, 128, 64, 0.125)
+    assert e.value.code == capi.MFA_ERR_INVALID_ARGUMENT
+
+
+def test_negative_extent_rejected():
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd(FAKE, FAKE, FAKE, FAKE, -1, 128, 64, 0.125)
+    assert e.value.code == capi.MFA_ERR_INVALID_ARGUMENT
+
+
+def test_empty_problem_is_a_noop():
+    capi.fwd(0, 0, 0, 0, 0, 128, 64, 0.125)
+    capi.fwd(0, 0, 0, 0, 4, 0, 64, 0.125, simple=True)
+
+
+def test_watchdog_limit_validated():
+    with pytest.raises(capi.MfaError) as e:
+        capi.set_watchdog_ns(10)
+    assert e.value.code == capi.MFA_ERR_INVALID_ARGUMENT
+    capi.set_watchdog_ns(2_000_000_000)
