@@ -10,14 +10,19 @@
 //   src/mini_flash_attention/flash_attn_cuda.cu:73-99     ScaleAccByRow / NormalizeAccByRow
 //
 // B200 structure (not a translation of the mma.sync kernel):
-//   warps 0..4*NQ-1 : softmax warpgroups; warpgroup i owns query tile i, one thread per row,
-//                     the row's 128 scores come from TMEM with tcgen05.ld (no shuffles).
-//   warp  4*NQ      : MMA issuer (one thread): S_i = Q_i K^T (SS form) and O_i += P_i V
-//                     (TS form, P read straight from TMEM, V consumed MN-major: no transpose).
-//   warp  4*NQ+1    : TMA producer: Q tiles once, then K and V blocks through STAGES slots.
+//   warps 0..8*NQ-1 : softmax warps. Query tile i is owned by warps 8i..8i+7; warp w reads
+//                     TMEM lane quadrant w%4 (32 rows, one row per thread) and column half
+//                     (w/4)%2 of the tile's 128 scores, so two threads share a row: they trade
+//                     their partial row max through shared memory each step and keep partial
+//                     row sums that are combined once, in the epilogue.
+//   warp  8*NQ      : MMA issuer (whole warp, one elected lane issues): S_i = Q_i K^T (SS
+//                     form) and O_i += P_i V (TS form: P straight from TMEM, V consumed
+//                     MN-major, so no transpose).
+//   warp  8*NQ+1    : TMA producer: Q tiles once, then K and V blocks through STAGES slots.
 // TMEM columns: S_i at 128*i, P_i (fp16 pairs) at 128*NQ + 64*i, O_i at 192*NQ + 64*i.
-// exp is exp2 with scale*log2(e) folded into one FMA; the running max is only raised when it
-// grows by more than kRescaleThreshold (log2 units), so O is rescaled in TMEM rarely.
+// exp is exp2 with scale*log2(e) folded into one FMA; 3 of every 8 pairs use an FMA-pipe
+// polynomial instead of MUFU. The running max is only raised when it grows by more than
+// kRescaleThreshold (log2 units), so O is rescaled in TMEM rarely.
 // Every mbarrier wait is bounded: on expiry the kernel records a status code, unwinds all
 // roles, drains its in-flight copies / MMAs and frees TMEM before returning.
 #pragma once
@@ -25,6 +30,7 @@
 #include <cuda.h>
 #include <cstdint>
 
+#include "mfa_exp2.cuh"
 #include "mfa_ptx.cuh"
 
 namespace mfa {
@@ -65,17 +71,18 @@ struct FwdConfig {
   static constexpr int kKeys = 128;       // keys per block (= S tile N)
   static constexpr int kHeadDim = 64;
   static constexpr int kTileBytes = kRows * kHeadDim * 2;  // 16 KiB, one TMA box
-  static constexpr int kSoftmaxWarps = 4 * NQ;
+  static constexpr int kSoftmaxWarps = 8 * NQ;   // two warps per TMEM lane quadrant and tile
   static constexpr int kMmaWarp = kSoftmaxWarps;
   static constexpr int kLoadWarp = kSoftmaxWarps + 1;
-  // With two softmax warpgroups the register file is rebalanced with setmaxnreg, which works
-  // per warpgroup: the MMA and TMA warps then form a full third warpgroup (2 warps idle).
-  // Per SM sub-partition: 216 + 216 + 72 regs x 32 lanes = 16128 <= 16384, and the totals
-  // match the launch allocation (384 x 168 = 256 x 216 + 128 x 72).
+  // With two query tiles (16 softmax warps) the register file is rebalanced with setmaxnreg,
+  // which works per warpgroup: the MMA and TMA warps then fill a fifth warpgroup (2 warps
+  // idle). 640 threads launch with 96 registers each (5 warps per SM sub-partition); after
+  // the split: 512 x 104 + 128 x 64 = 640 x 96, and per sub-partition 4 x 104 + 64 <= 512.
   static constexpr bool kRebalanceRegs = NQ == 2;
-  static constexpr int kThreads = kRebalanceRegs ? 32 * 12 : 32 * (kSoftmaxWarps + 2);
-  static constexpr int kSoftmaxRegs = 216;
-  static constexpr int kControlRegs = 72;
+  static constexpr int kThreads = kRebalanceRegs ? 32 * 20 : 32 * (kSoftmaxWarps + 2);
+  static constexpr int kLaunchRegs = 96;
+  static constexpr int kSoftmaxRegs = 104;
+  static constexpr int kControlRegs = 64;
 
   // shared memory (offsets from a 1024-aligned base; 128B swizzle atoms need 1024 alignment)
   static constexpr int kQOff = 0;
@@ -94,7 +101,11 @@ struct FwdConfig {
   static constexpr int kBarODone = kBarPFull + NQ;
   static constexpr int kBarDrain = kBarODone + NQ;
   static constexpr int kNumBars = kBarDrain + 1;
-  static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+  // partial row max / row sum exchange between the two threads of a row:
+  // [step parity][tile][column half][row] floats
+  static constexpr int kXchOff = kBarOff + kNumBars * 8;
+  static constexpr int kXchBytes = 2 * NQ * 2 * kRows * 4;
+  static constexpr int kTmemSlotOff = kXchOff + kXchBytes;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kSmemUsed = kAbortOff + 4;
   static constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for manual 1024 alignment
@@ -106,7 +117,12 @@ struct FwdConfig {
   static constexpr int kColO = 192 * NQ;
 
   static constexpr float kRescaleThreshold = 8.0f;
-  static_assert(!kRebalanceRegs || 2 * kSoftmaxRegs + kControlRegs <= 504, "register split");
+  // exp2 split: pair k of a row uses the polynomial when bit (k % 8) is set (3 of 8 pairs).
+  static constexpr uint32_t kPolyMask = 0x52u;
+  static_assert(!kRebalanceRegs ||
+                    4 * 32 * kSoftmaxRegs * 4 + 4 * 32 * kControlRegs == kThreads * kLaunchRegs,
+                "register split must use exactly the launch allocation");
+  static_assert(!kRebalanceRegs || 4 * kSoftmaxRegs + kControlRegs <= 512, "per sub-partition");
   static_assert(kColO + 64 * NQ <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
@@ -222,6 +238,9 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
   }
 }
 
+// Executed by the whole MMA warp: waits and descriptor arithmetic stay warp-uniform (uniform
+// datapath, no per-MMA register moves); one elected lane issues tcgen05.mma / commit. Issue
+// cost per MMA matters here: a 128x64x16 P.V step is only 32 tensor-core cycles.
 template <class Cfg>
 __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint32_t bars,
                                          uint32_t tmem, int nkb, const Watchdog& wd) {
@@ -231,68 +250,85 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
   const uint32_t sbase = smem_addr(smem);
   constexpr uint32_t kIdescS = idesc_f16_f32(128, 128, false);
   constexpr uint32_t kIdescO = idesc_f16_f32(128, 64, true);
+  // K-major Q / K tiles: SBO = 1024 (8-row swizzle atoms), LBO unused (16).
+  constexpr uint32_t kHiKMajor = smem_desc_hi(1024, kSwizzle128B);
+  // MN-major V tile (d contiguous): SBO = 1024 between 8-key groups, LBO = one tile (unused,
+  // the 64 d-columns are a single 128-byte swizzle atom).
+  constexpr uint32_t kHiMNMajor = smem_desc_hi(1024, kSwizzle128B);
+  const uint32_t q_lo = smem_desc_lo(sbase + Cfg::kQOff, 16);
+  const uint32_t k_lo = smem_desc_lo(sbase + Cfg::kKOff, 16);
+  const uint32_t v_lo = smem_desc_lo(sbase + Cfg::kVOff, Cfg::kTileBytes);
+  constexpr uint32_t kTileStep = Cfg::kTileBytes >> 4;
+  const bool leader = elect_one();
   bool issued_any = false;
 
-  if (!wait_single(bar(Cfg::kBarQFull), 0, wd, kSiteMmaQ)) goto unwind;
+  if (!wait_warp(bar(Cfg::kBarQFull), 0, wd, kSiteMmaQ)) goto unwind;
 
   for (int j = -1; j < nkb; ++j) {
     // ---- S_i[j+1] = Q_i K_{j+1}^T as soon as softmax_i has pulled S_i[j] into registers.
     if (j + 1 < nkb) {
       const int st1 = (j + 1) % ST;
       const uint32_t ph1 = static_cast<uint32_t>((j + 1) / ST) & 1u;
-      if (!wait_single(bar(Cfg::kBarKFull + st1), ph1, wd, kSiteMmaK)) goto unwind;
-      const uint32_t k_addr = sbase + Cfg::kKOff + st1 * Cfg::kTileBytes;
+      if (!wait_warp(bar(Cfg::kBarKFull + st1), ph1, wd, kSiteMmaK)) goto unwind;
+      const uint32_t kd = k_lo + st1 * kTileStep;
 #pragma unroll
       for (int i = 0; i < NQ; ++i) {
         if (j >= 0) {
-          if (!wait_single(bar(Cfg::kBarSFree + i), static_cast<uint32_t>(j) & 1u, wd,
-                           kSiteMmaSFree))
+          if (!wait_warp(bar(Cfg::kBarSFree + i), static_cast<uint32_t>(j) & 1u, wd,
+                         kSiteMmaSFree))
             goto unwind;
         }
         tc_fence_after();
-        const uint32_t q_addr = sbase + Cfg::kQOff + i * Cfg::kTileBytes;
-        const uint32_t d_tmem = tmem + Cfg::kColS + 128 * i;
+        if (leader) {
+          const uint32_t qd = q_lo + i * kTileStep;
+          const uint32_t d_tmem = tmem + Cfg::kColS + 128 * i;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a = smem_desc(q_addr + 32 * kk, 16, 1024, kSwizzle128B);
-          const uint64_t b = smem_desc(k_addr + 32 * kk, 16, 1024, kSwizzle128B);
-          mma_ss(d_tmem, a, b, kIdescS, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {  // 16 of the 64 head dims per MMA (32 bytes)
+            mma_ss(d_tmem, desc_join(qd + 2 * kk, kHiKMajor), desc_join(kd + 2 * kk, kHiKMajor),
+                   kIdescS, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar(Cfg::kBarSFull + i));
         }
+        __syncwarp();
         issued_any = true;
-        mma_commit(bar(Cfg::kBarSFull + i));
       }
-      mma_commit(bar(Cfg::kBarKEmpty + st1));
+      if (leader) mma_commit(bar(Cfg::kBarKEmpty + st1));
+      __syncwarp();
     }
     if (j < 0) continue;
     // ---- O_i += P_i[j] V_j once softmax_i has written P_i[j] (and rescaled O_i if needed).
     const int st = j % ST;
     const uint32_t ph = static_cast<uint32_t>(j / ST) & 1u;
-    if (!wait_single(bar(Cfg::kBarVFull + st), ph, wd, kSiteMmaV)) goto unwind;
-    const uint32_t v_addr = sbase + Cfg::kVOff + st * Cfg::kTileBytes;
+    if (!wait_warp(bar(Cfg::kBarVFull + st), ph, wd, kSiteMmaV)) goto unwind;
+    const uint32_t vd = v_lo + st * kTileStep;
 #pragma unroll
     for (int i = 0; i < NQ; ++i) {
-      if (!wait_single(bar(Cfg::kBarPFull + i), static_cast<uint32_t>(j) & 1u, wd, kSiteMmaPFull))
+      if (!wait_warp(bar(Cfg::kBarPFull + i), static_cast<uint32_t>(j) & 1u, wd, kSiteMmaPFull))
         goto unwind;
       tc_fence_after();
-      const uint32_t d_tmem = tmem + Cfg::kColO + 64 * i;
-      const uint32_t a_tmem = tmem + Cfg::kColP + 64 * i;
+      if (leader) {
+        const uint32_t d_tmem = tmem + Cfg::kColO + 64 * i;
+        const uint32_t a_tmem = tmem + Cfg::kColP + 64 * i;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        // 16 keys per MMA: two 8-row swizzle atoms of V (2 KiB).
-        const uint64_t b = smem_desc(v_addr + 2048 * kk, Cfg::kTileBytes, 1024, kSwizzle128B);
-        mma_ts(d_tmem, a_tmem + 8 * kk, b, kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: two 8-key swizzle atoms (2 KiB)
+          mma_ts(d_tmem, a_tmem + 8 * kk, desc_join(vd + 128 * kk, kHiMNMajor), kIdescO,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(Cfg::kBarODone + i));
       }
+      __syncwarp();
       issued_any = true;
-      mma_commit(bar(Cfg::kBarODone + i));
     }
-    mma_commit(bar(Cfg::kBarVEmpty + st));
+    if (leader) mma_commit(bar(Cfg::kBarVEmpty + st));
+    __syncwarp();
   }
   return;
 
 unwind:
   if (issued_any) {
-    // Let every MMA this thread issued finish before TMEM is released.
-    mma_commit(bar(Cfg::kBarDrain));
+    // Let every MMA this warp issued finish before TMEM is released.
+    if (leader) mma_commit(bar(Cfg::kBarDrain));
+    __syncwarp();
     drain_wait(bar(Cfg::kBarDrain), 0);
   }
 }
@@ -305,15 +341,22 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+  const int half = (warp >> 2) & 1;       // which 64 of the tile's 128 key columns
   const int row = quad * 32 + lane;       // row of the query tile == TMEM lane
   const uint32_t lane_bits = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t tS = tmem + lane_bits + Cfg::kColS + 128 * tile;
-  const uint32_t tP = tmem + lane_bits + Cfg::kColP + 64 * tile;
-  const uint32_t tO = tmem + lane_bits + Cfg::kColO + 64 * tile;
+  const uint32_t tS = tmem + lane_bits + Cfg::kColS + 128 * tile + 64 * half;
+  const uint32_t tP = tmem + lane_bits + Cfg::kColP + 64 * tile + 32 * half;
+  const uint32_t tO = tmem + lane_bits + Cfg::kColO + 64 * tile + 32 * half;
+  // partner exchange slots: xch[parity][tile][half][row]
+  float* xch = reinterpret_cast<float*>(smem + Cfg::kXchOff);
+  auto slot = [&](int parity, int h) {
+    return xch + ((parity * Cfg::NQ + tile) * 2 + h) * Cfg::kRows + row;
+  };
+  const int pair_bar = 1 + tile * 4 + quad;  // the two warps that share these 32 rows
   const float c = p.scale_log2;
 
-  float m_run = -INFINITY;  // running max of s*scale*log2(e)
-  float l_run = 0.0f;       // running sum of p (relative to m_run)
+  float m_run = -INFINITY;  // running max of s*scale*log2(e), identical in both threads
+  float l_run = 0.0f;       // this thread's partial sum of p over its column half
   bool ok = true;
 
   for (int j = 0; j < nkb; ++j) {
@@ -322,55 +365,70 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
       break;
     }
     tc_fence_after();
-    uint32_t sr[128];
-    tmem_ld128_sync(tS, sr);
+    uint32_t sr[64];
+    tmem_ld64_sync(tS, sr);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(bar(Cfg::kBarSFree + tile));
 
-    const int valid = p.n - j * Cfg::kKeys;
-    if (valid < Cfg::kKeys) {
+    const int valid = p.n - j * Cfg::kKeys - 64 * half;
+    if (valid < 64) {
 #pragma unroll
-      for (int k = 0; k < 128; ++k)
+      for (int k = 0; k < 64; ++k)
         if (k >= valid) sr[k] = __float_as_uint(-INFINITY);
     }
 
-    // Row max over the 128 scores of this block.
-    // Four independent 3-input max chains: 4 seeds + 15 x 8 pairs + 4 tail = 128 scores.
+    // Partial max over this half: four 3-input max chains (4 seeds, 7 x 8, 4 tail = 64).
     float mx[4];
 #pragma unroll
     for (int a = 0; a < 4; ++a) mx[a] = __uint_as_float(sr[a]);
 #pragma unroll
-    for (int k = 4; k < 124; k += 8) {
+    for (int k = 4; k < 60; k += 8) {
 #pragma unroll
       for (int a = 0; a < 4; ++a)
         mx[a] = max3(mx[a], __uint_as_float(sr[k + 2 * a]), __uint_as_float(sr[k + 2 * a + 1]));
     }
 #pragma unroll
-    for (int a = 0; a < 4; ++a) mx[a] = fmaxf(mx[a], __uint_as_float(sr[124 + a]));
-    const float m_blk = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;
+    for (int a = 0; a < 4; ++a) mx[a] = fmaxf(mx[a], __uint_as_float(sr[60 + a]));
+    const float pm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+    // Trade partial maxima with the partner thread (same row, other half). Slots alternate
+    // with the step parity so a partner one step ahead never overwrites an unread value.
+    *slot(j & 1, half) = pm;
+    named_bar_sync(pair_bar, 64);
+    const float m_blk = fmaxf(pm, *slot(j & 1, half ^ 1)) * c;
     const float m_new = fmaxf(m_run, m_blk);
-    // Raise the reference max only when some row of the warp grew past the threshold.
+    // Raise the reference max only when some row of the warp grew past the threshold. Both
+    // warps of a pair hold the same rows and values, so they take the same decision.
     const bool grow = __any_sync(0xffffffffu, m_new > m_run + Cfg::kRescaleThreshold);
     const float m_use = grow ? m_new : m_run;
     const float alpha = ex2_approx(m_run - m_use);  // 0 on the first block (m_run = -inf)
     const float neg_m = -m_use;
 
-    uint32_t pk[64];
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    // Scale-subtract and row sum run on packed pairs (fma/add .f32x2). Pairs whose index
+    // has its bit set in kPolyMask take exp2 from the FMA-pipe polynomial, the others from
+    // MUFU ex2, so both units work on every row.
+    const uint64_t c2 = f2_splat(c);
+    const uint64_t negm2 = f2_splat(neg_m);
+    uint32_t pk[32];
+    uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-    for (int k = 0; k < 64; k += 2) {
-      const float e0 = ex2_approx(fmaf(__uint_as_float(sr[2 * k + 0]), c, neg_m));
-      const float e1 = ex2_approx(fmaf(__uint_as_float(sr[2 * k + 1]), c, neg_m));
-      const float e2 = ex2_approx(fmaf(__uint_as_float(sr[2 * k + 2]), c, neg_m));
-      const float e3 = ex2_approx(fmaf(__uint_as_float(sr[2 * k + 3]), c, neg_m));
-      acc0 += e0;
-      acc1 += e1;
-      acc2 += e2;
-      acc3 += e3;
+    for (int k = 0; k < 32; ++k) {
+      const uint64_t x =
+          f2_fma(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])), c2, negm2);
+      float x0, x1, e0, e1;
+      f2_unpack(x, x0, x1);
+      if ((Cfg::kPolyMask >> (k & 7)) & 1u) {
+        exp2_poly_pair(x0, x1, e0, e1);
+      } else {
+        e0 = ex2_approx(x0);
+        e1 = ex2_approx(x1);
+      }
+      acc[k & 3] = f2_add(acc[k & 3], f2_pack(e0, e1));
       pk[k] = pack_half2(e0, e1);
-      pk[k + 1] = pack_half2(e2, e3);
     }
+    float acc0, acc1, acc2, acc3;
+    f2_unpack(f2_add(acc[0], acc[1]), acc0, acc1);
+    f2_unpack(f2_add(acc[2], acc[3]), acc2, acc3);
     l_run = l_run * alpha + ((acc0 + acc1) + (acc2 + acc3));
     m_run = m_use;
 
@@ -383,17 +441,13 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
       }
       tc_fence_after();
     }
-    tmem_st32(tP + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-    tmem_st32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+    tmem_st32(tP, pk);
     if (grow && j > 0) {
       uint32_t o[32];
+      tmem_ld32_sync(tO, o);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        tmem_ld32_sync(tO + 32 * h, o);
-#pragma unroll
-        for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-        tmem_st32(tO + 32 * h, o);
-      }
+      for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+      tmem_st32(tO, o);
     }
     tmem_wait_st();
     tc_fence_before();
@@ -406,34 +460,34 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     ok = wait_warp(bar(Cfg::kBarODone + tile), static_cast<uint32_t>(nkb - 1) & 1u, wd,
                    kSiteSoftOFinal);
   }
+  // Row sum = both halves' partial sums (every thread reaches this barrier, ok or not).
+  *slot(nkb & 1, half) = l_run;
+  named_bar_sync(pair_bar, 64);
+  const float l_row = l_run + *slot(nkb & 1, half ^ 1);
   uint8_t* stage = smem + Cfg::kQOff + tile * Cfg::kTileBytes;
   if (ok) {
     tc_fence_after();
-    const float inv_l = 1.0f / l_run;
+    const float inv_l = 1.0f / l_row;
+    uint32_t o[32];
+    tmem_ld32_sync(tO, o);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t o[32];
-      tmem_ld32_sync(tO + 32 * h, o);
+    for (int ch = 0; ch < 4; ++ch) {  // 4 chunks of 8 halves = 16 bytes each
+      uint32_t w[4];
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {  // 4 chunks of 8 halves = 16 bytes each
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          w[e] = pack_half2(__uint_as_float(o[8 * ch + 2 * e]) * inv_l,
-                            __uint_as_float(o[8 * ch + 2 * e + 1]) * inv_l);
-        }
-        const int chunk = 4 * h + ch;
-        const uint32_t dst =
-            smem_addr(stage + row * 128 + ((chunk ^ (row & 7)) << 4));
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]),
-                     "r"(w[2]), "r"(w[3])
-                     : "memory");
+      for (int e = 0; e < 4; ++e) {
+        w[e] = pack_half2(__uint_as_float(o[8 * ch + 2 * e]) * inv_l,
+                          __uint_as_float(o[8 * ch + 2 * e + 1]) * inv_l);
       }
+      const int chunk = 4 * half + ch;
+      const uint32_t dst = smem_addr(stage + row * 128 + ((chunk ^ (row & 7)) << 4));
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]),
+                   "r"(w[2]), "r"(w[3])
+                   : "memory");
     }
     fence_proxy_async_smem();
   }
-  named_bar_sync(1 + tile, 128);
-  if (ok && row == 0 && !*wd.abort) {
+  named_bar_sync(9 + tile, 256);
+  if (ok && half == 0 && row == 0 && !*wd.abort) {
     const int r0 = q_row0 + tile * Cfg::kRows;
     if (r0 < p.n) {
       tma_store_3d(&p.tm_o, smem_addr(stage), 0, r0, head);
@@ -472,8 +526,8 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
     }
     for (int i = 0; i < NQ; ++i) {
       mbar_init(bars + 8 * (Cfg::kBarSFull + i), 1);
-      mbar_init(bars + 8 * (Cfg::kBarSFree + i), 4);
-      mbar_init(bars + 8 * (Cfg::kBarPFull + i), 4);
+      mbar_init(bars + 8 * (Cfg::kBarSFree + i), 8);  // one arrive per softmax warp of tile i
+      mbar_init(bars + 8 * (Cfg::kBarPFull + i), 8);
       mbar_init(bars + 8 * (Cfg::kBarODone + i), 1);
     }
     mbar_init(bars + 8 * Cfg::kBarDrain, 1);
@@ -494,11 +548,11 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
     if (warp == Cfg::kLoadWarp) {
       if (lane == 0) load_role<Cfg>(p, smem, bars, head, q_row0, nkb, wd);
     } else if (warp == Cfg::kMmaWarp) {
-      if (lane == 0) mma_role<Cfg>(p, smem, bars, tmem, nkb, wd);
+      mma_role<Cfg>(p, smem, bars, tmem, nkb, wd);
     }
   } else {
     if constexpr (Cfg::kRebalanceRegs) setmaxnreg_inc<Cfg::kSoftmaxRegs>();
-    softmax_role<Cfg>(p, smem, bars, tmem, warp / 4, head, q_row0, nkb, wd);
+    softmax_role<Cfg>(p, smem, bars, tmem, warp / 8, head, q_row0, nkb, wd);
   }
   __syncwarp();
   tc_fence_before();

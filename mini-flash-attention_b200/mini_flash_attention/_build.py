@@ -34,7 +34,7 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + ["-O3", "-lineinfo", "-std=c++17", "-Xptxas", "-v"]
 
 LIB_SOURCES = [CSRC / "mfa_capi.cu"]
-LIB_DEPS = LIB_SOURCES + [CSRC / "mfa_fwd_kernel.cuh", CSRC / "mfa_ptx.cuh", INCLUDE / "mfa_b200.h"]
+LIB_DEPS = LIB_SOURCES + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "mfa_b200.h"]
 BINDING_SOURCES = [CSRC / "mfa_binding.cpp"]
 
 

@@ -11,7 +11,8 @@ Cases: the three shapes of the reference test (tests/test_forward.py:9-18: (1,2,
 like the long-sequence config (q,k ~ N(0,3^2): peaky softmax) and the short-sequence config
 (uniform[-1,1]) at sizes the oracle finishes in seconds.
 
-Usage (GPU box): python tests/golden/make_golden.py
+Usage (GPU box): python tests/golden/make_golden.py [--out PATH]
+(then copy the file to tests/golden/reference_outputs.npz and commit it with this script).
 """
 from __future__ import annotations
 
@@ -58,6 +59,11 @@ def input_digest(q, k, v) -> str:
 
 
 def main() -> None:
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", type=Path, default=OUT)
+    out_path = ap.parse_args().out
     sys.path.insert(0, str(ROOT))
     import torch
 
@@ -75,8 +81,8 @@ def main() -> None:
             torch.cuda.synchronize()
             arrays[f"{name}__{kern}"] = out.cpu().numpy()
             print(name, kern, float(out.float().abs().max()))
-    np.savez_compressed(OUT, **arrays)
-    print("wrote", OUT)
+    np.savez_compressed(out_path, **arrays)
+    print("wrote", out_path)
 
 
 if __name__ == "__main__":

@@ -105,11 +105,17 @@ def test_forward_wmma_handles_n_multiple_of_64():
 
 
 def test_v_scaling_is_exact():
-    # P.(2V) == 2 (P.V) in every rounding step: the outputs must be bit-identical x2.
+    # Doubling V doubles every product and every partial sum exactly, so every output in the
+    # fp16 normal range must be exactly twice the original. Outputs below 2^-14 are fp16
+    # subnormals: there the first result was rounded to a coarser grid than its double, so
+    # they may differ by one subnormal step (2^-24), as they do for the reference kernel.
     q, k, v = (randn_cuda((2, 2, 1024, 64), 40 + i) for i in range(3))
     a = mfa.forward(q, k, v)
     b = mfa.forward(q, k, v * 2)
-    assert torch.equal(b, a * 2)
+    normal = a.abs() >= 2.0 ** -14
+    assert normal.float().mean() > 0.99
+    assert torch.equal(b[normal], a[normal] * 2)
+    assert (b.float() - 2 * a.float()).abs().max() <= 2.0 ** -23
 
 
 def test_key_permutation_invariance():
