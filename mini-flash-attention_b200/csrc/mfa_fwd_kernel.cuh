@@ -61,6 +61,7 @@ enum WaitSite : int {
   kSiteSoftSFull = 8,
   kSiteSoftODone = 9,
   kSiteSoftOFinal = 10,
+  kSiteSoftExpTok = 11,
 };
 
 template <int NQ_, int STAGES_>
@@ -99,7 +100,9 @@ struct FwdConfig {
   static constexpr int kBarSFree = kBarSFull + NQ;
   static constexpr int kBarPFull = kBarSFree + NQ;
   static constexpr int kBarODone = kBarPFull + NQ;
-  static constexpr int kBarDrain = kBarODone + NQ;
+  // exp-phase tokens: with two tiles their exp loops take turns (tile 0 first)
+  static constexpr int kBarExpTok = kBarODone + NQ;
+  static constexpr int kBarDrain = kBarExpTok + 2;
   static constexpr int kNumBars = kBarDrain + 1;
   // partial row max / row sum exchange between the two threads of a row:
   // [step parity][tile][column half][row] floats
@@ -117,8 +120,13 @@ struct FwdConfig {
   static constexpr int kColO = 192 * NQ;
 
   static constexpr float kRescaleThreshold = 8.0f;
-  // exp2 split: pair k of a row uses the polynomial when bit (k % 8) is set (3 of 8 pairs).
-  static constexpr uint32_t kPolyMask = 0x52u;
+  // exp2 split: pair k of a row uses the polynomial when bit (k % 8) is set (1 of 8 pairs;
+  // the polynomial costs ~5 issue slots per element against 1 for MUFU, so a small share
+  // relieves MUFU without starving issue).
+  static constexpr uint32_t kPolyMask = 0x10u;
+  // With two tiles, their exp loops alternate (mbarrier tokens), so one tile's TMEM traffic,
+  // max exchange and barrier waits overlap the other tile's MUFU / FMA work.
+  static constexpr bool kPingPong = false;
   static_assert(!kRebalanceRegs ||
                     4 * 32 * kSoftmaxRegs * 4 + 4 * 32 * kControlRegs == kThreads * kLaunchRegs,
                 "register split must use exactly the launch allocation");
@@ -358,6 +366,8 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   float m_run = -INFINITY;  // running max of s*scale*log2(e), identical in both threads
   float l_run = 0.0f;       // this thread's partial sum of p over its column half
   bool ok = true;
+  // Tile 1 hands tile 0 the first exp turn.
+  if (Cfg::kPingPong && tile == 1 && lane == 0) mbar_arrive(bar(Cfg::kBarExpTok + 0));
 
   for (int j = 0; j < nkb; ++j) {
     if (!wait_warp(bar(Cfg::kBarSFull + tile), static_cast<uint32_t>(j) & 1u, wd, kSiteSoftSFull)) {
@@ -402,7 +412,16 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     const bool grow = __any_sync(0xffffffffu, m_new > m_run + Cfg::kRescaleThreshold);
     const float m_use = grow ? m_new : m_run;
     const float alpha = ex2_approx(m_run - m_use);  // 0 on the first block (m_run = -inf)
-    const float neg_m = -m_use;
+    float neg_m = -m_use;
+    if constexpr (Cfg::kPingPong) {
+      if (!wait_warp(bar(Cfg::kBarExpTok + tile), static_cast<uint32_t>(j) & 1u, wd,
+                     kSiteSoftExpTok)) {
+        ok = false;
+        break;
+      }
+      // Pin the exp loop below the token wait: it depends on neg_m "produced" here.
+      asm volatile("" : "+f"(neg_m)::"memory");
+    }
 
     // Scale-subtract and row sum run on packed pairs (fma/add .f32x2). Pairs whose index
     // has its bit set in kPolyMask take exp2 from the FMA-pipe polynomial, the others from
@@ -431,6 +450,12 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     f2_unpack(f2_add(acc[2], acc[3]), acc2, acc3);
     l_run = l_run * alpha + ((acc0 + acc1) + (acc2 + acc3));
     m_run = m_use;
+    if constexpr (Cfg::kPingPong) {
+      // Keep the exp results above the hand-over, then pass the turn to the other tile.
+      regs_ready(pk, l_run);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(Cfg::kBarExpTok + (tile ^ 1)));
+    }
 
     // P_i and O_i are free once the previous O_i += P_i V has completed.
     if (j > 0) {
@@ -530,6 +555,8 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
       mbar_init(bars + 8 * (Cfg::kBarPFull + i), 8);
       mbar_init(bars + 8 * (Cfg::kBarODone + i), 1);
     }
+    mbar_init(bars + 8 * (Cfg::kBarExpTok + 0), 8);
+    mbar_init(bars + 8 * (Cfg::kBarExpTok + 1), 8);
     mbar_init(bars + 8 * Cfg::kBarDrain, 1);
     mbar_init_fence();
   }

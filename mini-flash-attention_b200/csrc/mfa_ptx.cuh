@@ -316,6 +316,18 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
       : "memory");
 }
 
+// Compiler-only ordering point: every value below counts as used here, so the instructions
+// that produce them cannot be sunk past the next volatile asm (e.g. an mbarrier arrive).
+__device__ __forceinline__ void regs_ready(const uint32_t (&r)[32], float f) {
+  asm volatile(
+      "" ::"r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+      "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+      "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
+      "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "f"(f)
+      : "memory");
+}
+
 // One lane of the (converged) warp gets true.
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred;
