@@ -50,6 +50,7 @@ PUBLISHED_TFLOPS = 4 * 8 * 8192 ** 2 * 64 / (PUBLISHED_TFLOPS * 1e-3) / 1e12
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 L2_FLUSH_MB = 256
 INPUT_BUFFERS = 4
+E2E_CHUNKS = 2  # measured best on this box: opposite-direction copies slow each other
 
 WORKLOADS = {
     "b1h8n8192": dict(B=1, H=8, N=8192, dist="normal", qk_scale=1.0, scaling="weak"),
@@ -281,27 +282,20 @@ def run_ours(args, wl) -> dict | None:
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         total_ms = max_over_ranks(sum(step_ms), world)
 
-        # ---- end to end: pinned host inputs -> device -> forward -> host output
+        # ---- end to end: pinned host q, k, v -> device -> forward -> pinned host output,
+        # through the public host-buffer API (copies of batch*head slices overlap kernels)
         host_in = [x.cpu().pin_memory() for x in inputs[0]]
-        dev_in = [torch.empty_like(x) for x in inputs[0]]
         host_out = torch.empty(inputs[0][0].shape, dtype=torch.float16).pin_memory()
         e2e_steps = max(args.steps, 3)
+        chunks = min(bh, E2E_CHUNKS)
         for _ in range(2):
-            for h, d_ in zip(host_in, dev_in):
-                d_.copy_(h, non_blocking=True)
-            host_out.copy_(fwd(*dev_in), non_blocking=True)
+            mfa.forward_pinned(*host_in, out=host_out, chunks=chunks, device=dev)
         torch.cuda.synchronize(dev)
         barrier(world)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        t0 = time.perf_counter()
         for _ in range(e2e_steps):
-            for h, d_ in zip(host_in, dev_in):
-                d_.copy_(h, non_blocking=True)
-            host_out.copy_(fwd(*dev_in), non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+            mfa.forward_pinned(*host_in, out=host_out, chunks=chunks, device=dev)
+        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
         barrier(world)
 
     if world > 1:
@@ -361,8 +355,9 @@ def run_ours(args, wl) -> dict | None:
         "e2e": {
             "value": round(e2e_value, 3), "unit": UNIT,
             "h2d_bytes_per_step": bytes_in, "d2h_bytes_per_step": bytes_out,
-            "path": "pinned host q,k,v -> cudaMemcpyAsync -> mini_flash_attention.forward -> "
-                    "pinned host out, one stream",
+            "path": "mini_flash_attention.forward_pinned: pinned host q,k,v -> H2D / forward / "
+                    "D2H of batch*head slices pipelined on 3 streams -> pinned host out",
+            "timing": "host wall clock around the synchronous calls, max over ranks",
         },
         "gpu_launches": args.steps,
         "clocks": clocks,

@@ -68,6 +68,26 @@ torch::Tensor forward_impl(const torch::Tensor& q, const torch::Tensor& k, const
   return out;
 }
 
+// Same as forward, writing into a caller-provided contiguous fp16 tensor of q's shape
+// (used by the pipelined host-buffer path to fill slices of one device buffer).
+void flash_attn_forward_into(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
+                             bool causal) {
+  check_forward_inputs(q, k, v);
+  TORCH_CHECK(out.is_cuda() && out.device() == q.device(), "out must be on q's device");
+  TORCH_CHECK(out.scalar_type() == torch::kFloat16, "out must be float16");
+  TORCH_CHECK(out.is_contiguous(), "out must be contiguous");
+  TORCH_CHECK(out.sizes() == q.sizes(), "out must have the same shape as q");
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  const int64_t BH = q.dim() == 4 ? q.size(0) * q.size(1) : q.size(0);
+  const int64_t N = q.size(-2);
+  const int64_t D = q.size(-1);
+  const float scale = 1.0f / std::sqrt(static_cast<float>(D));
+  const int rc = mfa_fwd_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), BH, N,
+                             static_cast<int32_t>(D), scale, causal ? 1 : 0,
+                             static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
+  if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
+}
+
 torch::Tensor flash_attn_forward(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal) {
   return forward_impl(q, k, v, causal, &mfa_fwd_f16);
 }
@@ -83,5 +103,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward", &flash_attn_forward, "Mini Flash Attention forward (sm_100a tcgen05)");
   m.def("forward_wmma", &flash_attn_forward_wmma,
         "Mini Flash Attention forward, single-tile sm_100a kernel (replaces the WMMA path)");
+  m.def("forward_into", &flash_attn_forward_into,
+        "Mini Flash Attention forward into a preallocated output tensor");
   m.def("version", []() { return std::string(mfa_version()); });
 }

@@ -39,6 +39,8 @@ struct DeviceState {
   int error = MFA_OK;
   std::string message;
   int* status_ptr = nullptr;
+  int num_sms = 0;
+  cudaMemPool_t pool = nullptr;  // split-mode scratch; keeps its memory between calls
 };
 DeviceState g_devices[kMaxDevices];
 
@@ -89,13 +91,29 @@ int prepare_device(int dev) {
                    std::to_string(dev) + " is sm_" + std::to_string(major) + std::to_string(minor);
       return;
     }
-    e = cudaFuncSetAttribute(mfa_fwd_kernel<FullKernel::NQ, FullKernel::STAGES>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, FullKernel::kSmemBytes);
+    e = cudaDeviceGetAttribute(&ds.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(mfa_fwd_kernel<FullKernel::NQ, FullKernel::STAGES>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, FullKernel::kSmemBytes);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(mfa_fwd_kernel<SimpleKernel::NQ, SimpleKernel::STAGES>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                SimpleKernel::kSmemBytes);
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status_ptr), g_device_status);
+    if (e == cudaSuccess) {
+      // A private stream-ordered pool for the split-mode partial results: the scratch is
+      // allocated and freed on the caller's stream around each launch, and the pool keeps
+      // the memory mapped so that later calls do not pay for mapping it again.
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      e = cudaMemPoolCreate(&ds.pool, &props);
+      if (e == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        e = cudaMemPoolSetAttribute(ds.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      }
+    }
     if (e != cudaSuccess) {
       ds.error = MFA_ERR_CUDA;
       ds.message = std::string("CUDA error: ") + cudaGetErrorString(e) + " (device set-up)";
@@ -122,6 +140,10 @@ int encode_bhnd(CUtensorMap* map, const void* base, int64_t n, int64_t bh) {
   return MFA_OK;
 }
 
+// Persistent launch: one CTA per SM (or fewer for small problems). When whole query blocks
+// divide badly over the SMs (more than 3% idle in the last wave), the key dimension is split
+// too and a merge kernel combines the pieces; the partial results live in a stream-ordered
+// scratch allocation freed on the same stream.
 template <class Cfg>
 int launch_forward(const void* q, const void* k, const void* v, void* out, int64_t bh, int64_t n,
                    float scale, cudaStream_t stream) {
@@ -137,20 +159,62 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
   if ((rc = encode_bhnd(&p.tm_k, k, n, bh)) != MFA_OK) return rc;
   if ((rc = encode_bhnd(&p.tm_v, v, n, bh)) != MFA_OK) return rc;
   if ((rc = encode_bhnd(&p.tm_o, out, n, bh)) != MFA_OK) return rc;
-  const int64_t rows_per_cta = static_cast<int64_t>(Cfg::kRows) * Cfg::NQ;
-  const int64_t q_blocks = (n + rows_per_cta - 1) / rows_per_cta;
+  const int64_t q_blocks = (n + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
+  const int64_t nkb = (n + Cfg::kKeys - 1) / Cfg::kKeys;
+  const int64_t units = q_blocks * bh;
+  if (units > (int64_t(1) << 40) / nkb)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  const int64_t sms = g_devices[dev].num_sms;
+  if (units > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  int64_t ctas = units < sms ? units : sms;
+  int split = 0;
+  if (units % sms != 0 && units < 32 * sms) {
+    // idle fraction of the last wave if only whole query blocks are handed out
+    const double waves = static_cast<double>(units) / sms;
+    const double busy = waves / static_cast<double>((units + sms - 1) / sms);
+    if (busy < 0.97) {
+      split = 1;
+      ctas = units * nkb < sms ? units * nkb : sms;
+    }
+  }
+  // every CTA's work must stay below 2^31 steps (32-bit step counters in the kernel)
+  if ((split ? units * nkb / ctas : (units + ctas - 1) / ctas * nkb) >= 0x7fffffffLL)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
   p.n = static_cast<int>(n);
   p.bh = static_cast<int>(bh);
   p.q_blocks = static_cast<int>(q_blocks);
+  p.nkb = static_cast<int>(nkb);
+  p.split = split;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.timeout_ns = g_watchdog_ns;
   p.status = g_devices[dev].status_ptr;
-
-  const int64_t grid = q_blocks * bh;
-  if (grid > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  p.workspace = nullptr;
+  if (split) {
+    const size_t bytes = static_cast<size_t>(2 * ctas) * Cfg::kSlotFloats * sizeof(float);
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&p.workspace), bytes,
+                                g_devices[dev].pool, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaMallocFromPoolAsync (split workspace)");
+  }
   mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES>
-      <<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+      <<<static_cast<unsigned>(ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   e = cudaGetLastError();
+  if (e == cudaSuccess && split) {
+    MergeParams mp;
+    mp.out = out;
+    mp.workspace = p.workspace;
+    mp.n = p.n;
+    mp.bh = p.bh;
+    mp.q_blocks = p.q_blocks;
+    mp.nkb = p.nkb;
+    mp.ctas = static_cast<int>(ctas);
+    mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats>
+        <<<static_cast<unsigned>(ctas), Cfg::kRowsPerUnit, 0, stream>>>(mp);
+    e = cudaGetLastError();
+  }
+  if (split) {
+    const cudaError_t ef = cudaFreeAsync(p.workspace, stream);
+    if (e == cudaSuccess) e = ef;
+  }
   if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
   return MFA_OK;
 }

@@ -1,0 +1,113 @@
+// Shared pieces of the attention kernels: launch parameters, the device status codes and the
+// bounded mbarrier waits (watchdog) every role uses.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+#include "mfa_ptx.cuh"
+
+namespace mfa {
+
+struct FwdParams {
+  CUtensorMap tm_q;  // [BH][N][64] fp16, box 64 x 128 x 1, 128B swizzle
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  CUtensorMap tm_o;
+  int n;                      // sequence length (keys == queries)
+  int bh;                     // batch * heads
+  int q_blocks;               // query blocks per head: ceil(n / rows per CTA pass)
+  int nkb;                    // key blocks per row: ceil(n / keys per block)
+  // Persistent schedule: the units (head, query block, key block), in that row-major order,
+  // are cut into gridDim.x contiguous ranges, one per CTA. split == 0 puts the cuts on whole
+  // query blocks; split == 1 cuts anywhere and a query block processed in pieces by several
+  // CTAs leaves partial results (unnormalised O, row max, row sum) in `workspace`, which the
+  // merge kernel combines.
+  int split;
+  float scale_log2;           // softmax scale * log2(e)
+  unsigned long long timeout_ns;  // per-wait watchdog limit
+  int* status;                // device status word (0 = ok)
+  float* workspace;           // split mode: 2 * gridDim.x partial-result slots
+};
+
+// Status codes written to FwdParams::status by the watchdog: kStatusTimeoutBase + site.
+constexpr int kStatusTimeoutBase = 0x100;
+enum WaitSite : int {
+  kSiteLoadKEmpty = 1,
+  kSiteLoadVEmpty = 2,
+  kSiteMmaQ = 3,
+  kSiteMmaK = 4,
+  kSiteMmaSFree = 5,
+  kSiteMmaV = 6,
+  kSiteMmaPFull = 7,
+  kSiteSoftSFull = 8,
+  kSiteSoftODone = 9,
+  kSiteSoftOFinal = 10,
+  kSiteSoftExpTok = 11,
+  kSiteMmaStall = 12,
+  kSiteLoadQEmpty = 13,
+  kSiteSoftXch = 14,
+  kSiteSoftStage = 15,
+};
+
+struct Watchdog {
+  volatile int* abort;
+  int* status;
+  unsigned long long timeout_ns;
+
+  __device__ void trip(int site) const {
+    *abort = 1;
+    atomicCAS(status, 0, kStatusTimeoutBase + site);
+  }
+};
+
+// Wait by one thread. Returns false if the CTA is aborting or this wait timed out.
+__device__ __forceinline__ bool wait_single(uint32_t bar, uint32_t parity, const Watchdog& wd,
+                                            int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 0) {
+      if (*wd.abort) return false;
+      if (global_timer_ns() - t0 > wd.timeout_ns) {
+        wd.trip(site);
+        return false;
+      }
+    }
+  }
+}
+
+// Warp-collective wait: every lane polls, the warp leaves together with one verdict.
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, const Watchdog& wd,
+                                          int site) {
+  const int lane = threadIdx.x & 31;
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    const bool ok = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    if ((it & 15u) == 15u) {
+      int stop = 0;
+      if (lane == 0) {
+        if (t0 == 0) t0 = global_timer_ns();
+        if (*wd.abort) {
+          stop = 1;
+        } else if (global_timer_ns() - t0 > wd.timeout_ns) {
+          wd.trip(site);
+          stop = 1;
+        }
+      }
+      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+    }
+  }
+}
+
+// Bounded drain used only while unwinding: ignores the abort flag.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > 200000000ull) return;  // 200 ms
+  }
+}
+
+}  // namespace mfa

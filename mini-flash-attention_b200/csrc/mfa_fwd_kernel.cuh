@@ -1,6 +1,7 @@
 // FlashAttention forward for sm_100a: fp16 Q/K/V in [BH, N, 64], fp32 online softmax,
-// fp16 output. One CTA owns NQ query tiles of 128 rows of one (batch*head) and streams the
-// whole key/value sequence of that head through a TMA + mbarrier ring.
+// fp16 output. Persistent: one CTA per SM walks a contiguous range of work units
+// (head, query block of 128*NQ rows, key block of 128 keys) and streams K/V through a TMA +
+// mbarrier ring that runs across unit boundaries.
 //
 // Reference semantics (lavawolfiee/mini-flash-attention):
 //   src/mini_flash_attention/flash_attn_cuda.cu:190-368   FlashAttnCuteKernel (per Q tile
@@ -18,57 +19,35 @@
 //   warp  8*NQ      : MMA issuer (whole warp, one elected lane issues): S_i = Q_i K^T (SS
 //                     form) and O_i += P_i V (TS form: P straight from TMEM, V consumed
 //                     MN-major, so no transpose).
-//   warp  8*NQ+1    : TMA producer: Q tiles once, then K and V blocks through STAGES slots.
+//   warp  8*NQ+1    : TMA producer: the Q tiles of each unit (two Q buffers, so the next
+//                     unit's Q loads while this one runs), then K and V blocks.
 // TMEM columns: S_i at 128*i, P_i (fp16 pairs) at 128*NQ + 64*i, O_i at 192*NQ + 64*i.
-// exp is exp2 with scale*log2(e) folded into one FMA; 3 of every 8 pairs use an FMA-pipe
+// exp is exp2 with scale*log2(e) folded into one FMA; 1 of every 8 pairs uses an FMA-pipe
 // polynomial instead of MUFU. The running max is only raised when it grows by more than
 // kRescaleThreshold (log2 units), so O is rescaled in TMEM rarely.
+// Work split: see FwdParams::split. A unit range that covers a whole query block ends with
+// O / l stored as fp16 by TMA; a piece of a query block leaves fp32 partial results in the
+// workspace for mfa_merge_kernel.
 // Every mbarrier wait is bounded: on expiry the kernel records a status code, unwinds all
 // roles, drains its in-flight copies / MMAs and frees TMEM before returning.
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cstdint>
 
+#include "mfa_common.cuh"
 #include "mfa_exp2.cuh"
 #include "mfa_ptx.cuh"
 
 namespace mfa {
-
-struct FwdParams {
-  CUtensorMap tm_q;  // [BH][N][64] fp16, box 64 x 128 x 1, 128B swizzle
-  CUtensorMap tm_k;
-  CUtensorMap tm_v;
-  CUtensorMap tm_o;
-  int n;                      // sequence length (keys == queries)
-  int bh;                     // batch * heads
-  int q_blocks;               // ceil(n / (128 * NQ))
-  float scale_log2;           // softmax scale * log2(e)
-  unsigned long long timeout_ns;  // per-wait watchdog limit
-  int* status;                // device status word (0 = ok)
-};
-
-// Status codes written to FwdParams::status by the watchdog: kStatusTimeoutBase + site.
-constexpr int kStatusTimeoutBase = 0x100;
-enum WaitSite : int {
-  kSiteLoadKEmpty = 1,
-  kSiteLoadVEmpty = 2,
-  kSiteMmaQ = 3,
-  kSiteMmaK = 4,
-  kSiteMmaSFree = 5,
-  kSiteMmaV = 6,
-  kSiteMmaPFull = 7,
-  kSiteSoftSFull = 8,
-  kSiteSoftODone = 9,
-  kSiteSoftOFinal = 10,
-  kSiteSoftExpTok = 11,
-};
 
 template <int NQ_, int STAGES_>
 struct FwdConfig {
   static constexpr int NQ = NQ_;
   static constexpr int STAGES = STAGES_;
   static constexpr int kRows = 128;       // query rows per tile (= MMA M)
+  static constexpr int kRowsPerUnit = kRows * NQ;
   static constexpr int kKeys = 128;       // keys per block (= S tile N)
   static constexpr int kHeadDim = 64;
   static constexpr int kTileBytes = kRows * kHeadDim * 2;  // 16 KiB, one TMA box
@@ -86,13 +65,14 @@ struct FwdConfig {
   static constexpr int kControlRegs = 64;
 
   // shared memory (offsets from a 1024-aligned base; 128B swizzle atoms need 1024 alignment)
-  static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + NQ * kTileBytes;
+  static constexpr int kQOff = 0;                              // two Q buffers of NQ tiles
+  static constexpr int kKOff = kQOff + 2 * NQ * kTileBytes;
   static constexpr int kVOff = kKOff + STAGES * kTileBytes;
   static constexpr int kBarOff = kVOff + STAGES * kTileBytes;
   // barrier indices
-  static constexpr int kBarQFull = 0;
-  static constexpr int kBarKFull = 1;
+  static constexpr int kBarQFull = 0;                 // [2]
+  static constexpr int kBarQEmpty = 2;                // [2]
+  static constexpr int kBarKFull = 4;
   static constexpr int kBarKEmpty = kBarKFull + STAGES;
   static constexpr int kBarVFull = kBarKEmpty + STAGES;
   static constexpr int kBarVEmpty = kBarVFull + STAGES;
@@ -100,14 +80,15 @@ struct FwdConfig {
   static constexpr int kBarSFree = kBarSFull + NQ;
   static constexpr int kBarPFull = kBarSFree + NQ;
   static constexpr int kBarODone = kBarPFull + NQ;
-  // exp-phase tokens: with two tiles their exp loops take turns (tile 0 first)
-  static constexpr int kBarExpTok = kBarODone + NQ;
-  static constexpr int kBarDrain = kBarExpTok + 2;
+  // Row-sum exchange between the two warps of a lane quadrant at the end of a unit (count 2,
+  // [tile][quad]); an mbarrier rather than a named barrier, so the wait stays bounded.
+  static constexpr int kBarXchSum = kBarODone + NQ;
+  static constexpr int kBarStage = kBarXchSum + NQ * 4;  // [tile]: output staging written
+  static constexpr int kBarDrain = kBarStage + NQ;
   static constexpr int kNumBars = kBarDrain + 1;
-  // partial row max / row sum exchange between the two threads of a row:
-  // [step parity][tile][column half][row] floats
+  // partner exchange of the final row sums: [tile][column half][row] floats
   static constexpr int kXchOff = kBarOff + kNumBars * 8;
-  static constexpr int kXchBytes = 2 * NQ * 2 * kRows * 4;
+  static constexpr int kXchBytes = NQ * 2 * kRows * 4;
   static constexpr int kTmemSlotOff = kXchOff + kXchBytes;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kSmemUsed = kAbortOff + 4;
@@ -119,14 +100,15 @@ struct FwdConfig {
   static constexpr int kColP = 128 * NQ;
   static constexpr int kColO = 192 * NQ;
 
+  // one partial-result slot: O[rows][64] fp32 (unnormalised), then m[rows], l[rows]
+  static constexpr int kSlotFloats = kRowsPerUnit * (kHeadDim + 2);
+
   static constexpr float kRescaleThreshold = 8.0f;
   // exp2 split: pair k of a row uses the polynomial when bit (k % 8) is set (1 of 8 pairs;
   // the polynomial costs ~5 issue slots per element against 1 for MUFU, so a small share
   // relieves MUFU without starving issue).
   static constexpr uint32_t kPolyMask = 0x10u;
-  // With two tiles, their exp loops alternate (mbarrier tokens), so one tile's TMEM traffic,
-  // max exchange and barrier waits overlap the other tile's MUFU / FMA work.
-  static constexpr bool kPingPong = false;
+
   static_assert(!kRebalanceRegs ||
                     4 * 32 * kSoftmaxRegs * 4 + 4 * 32 * kControlRegs == kThreads * kLaunchRegs,
                 "register split must use exactly the launch allocation");
@@ -135,69 +117,90 @@ struct FwdConfig {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-struct Watchdog {
-  volatile int* abort;
-  int* status;
-  unsigned long long timeout_ns;
+// ---------------------------------------------------------------- unit schedule
+// Range of CTA `cta` of `ctas` over the row-major units (head, query block, key block).
+__host__ __device__ inline void cta_range(long long units, int nkb, int split, int cta, int ctas,
+                                          long long& begin, long long& end) {
+  if (split) {
+    const long long total = units * nkb;
+    begin = total * cta / ctas;
+    end = total * (cta + 1) / ctas;
+  } else {
+    begin = units * cta / ctas * nkb;
+    end = units * (cta + 1) / ctas * nkb;
+  }
+}
 
-  __device__ void trip(int site) const {
-    *abort = 1;
-    atomicCAS(status, 0, kStatusTimeoutBase + site);
+// Walks the steps (one key block of one query block each) of this CTA's work in order. Two
+// orders, chosen by FwdParams::split:
+//   split == 0: whole query blocks u = cta, cta + ctas, cta + 2 ctas, ... so that the CTAs
+//               running at the same time work on neighbouring query blocks, mostly of the
+//               same head, and its K/V blocks are read from L2 by all of them;
+//   split == 1: the contiguous range cta_range() (a head's K/V then fits in L2 anyway: split
+//               mode is only chosen when there are few query blocks).
+// Six 32-bit words of state: it is live across the softmax loop, where registers are scarce
+// (the launcher guarantees fewer than 2^31 units and steps per CTA). In split mode only the
+// range's first segment can start inside a query block and only its last can stop inside one.
+struct StepCursor {
+  int u;        // current query block, row-major over (head, query block)
+  int j;        // current key block
+  int j0, j1;   // key blocks [j0, j1) of u handled in this segment
+  int rem;      // split: steps after this segment; whole blocks: query blocks after this one
+  int seg_idx;  // index of the current segment
+
+  __device__ void init(const FwdParams& p) {
+    const long long units = static_cast<long long>(p.bh) * p.q_blocks;
+    seg_idx = 0;
+    if (!p.split) {
+      u = static_cast<int>(blockIdx.x);
+      j = j0 = 0;
+      j1 = u < units ? p.nkb : 0;
+      rem = u < units ? static_cast<int>((units - 1 - u) / gridDim.x) : 0;
+      return;
+    }
+    long long b, e;
+    cta_range(units, p.nkb, 1, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), b, e);
+    if (b >= e) {
+      u = j = j0 = j1 = rem = 0;
+      return;
+    }
+    const long long uu = b / p.nkb;
+    u = static_cast<int>(uu);
+    j0 = j = static_cast<int>(b - uu * p.nkb);
+    const long long len = e - b;
+    j1 = len < static_cast<long long>(p.nkb - j0) ? j0 + static_cast<int>(len) : p.nkb;
+    rem = static_cast<int>(len - (j1 - j0));
+  }
+  __device__ bool valid() const { return j < j1; }
+  __device__ bool first_step() const { return j == j0; }
+  __device__ bool last_step() const { return j == j1 - 1; }
+  __device__ bool first_of_range() const { return seg_idx == 0; }
+  __device__ bool whole(int nkb) const { return j0 == 0 && j1 == nkb; }
+  // Advance to the next segment (the softmax warps walk a segment with their own counter).
+  __device__ void next_segment(const FwdParams& p) {
+    j = j1 - 1;
+    step(p);
+  }
+  __device__ void step(const FwdParams& p) {
+    if (++j >= j1 && rem > 0) {
+      if (p.split) {
+        ++u;
+        j1 = rem < p.nkb ? rem : p.nkb;
+        rem -= j1;
+      } else {
+        u += static_cast<int>(gridDim.x);
+        j1 = p.nkb;
+        --rem;
+      }
+      j = j0 = 0;
+      ++seg_idx;
+    }
   }
 };
 
-// Wait by one thread. Returns false if the CTA is aborting or this wait timed out.
-__device__ __forceinline__ bool wait_single(uint32_t bar, uint32_t parity, const Watchdog& wd,
-                                            int site) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 15u) == 0) {
-      if (*wd.abort) return false;
-      if (global_timer_ns() - t0 > wd.timeout_ns) {
-        wd.trip(site);
-        return false;
-      }
-    }
-  }
-}
-
-// Warp-collective wait: every lane polls, the warp leaves together with one verdict.
-__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, const Watchdog& wd,
-                                          int site) {
-  const int lane = threadIdx.x & 31;
-  uint64_t t0 = 0;
-  for (uint32_t it = 0;; ++it) {
-    const bool ok = mbar_try_wait(bar, parity);
-    if (__all_sync(0xffffffffu, ok)) return true;
-    if ((it & 15u) == 15u) {
-      int stop = 0;
-      if (lane == 0) {
-        if (t0 == 0) t0 = global_timer_ns();
-        if (*wd.abort) {
-          stop = 1;
-        } else if (global_timer_ns() - t0 > wd.timeout_ns) {
-          wd.trip(site);
-          stop = 1;
-        }
-      }
-      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
-    }
-  }
-}
-
-// Bounded drain used only while unwinding: ignores the abort flag.
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - t0 > 200000000ull) return;  // 200 ms
-  }
-}
-
 template <class Cfg>
 __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uint32_t bars,
-                                          int head, int q_row0, int nkb, const Watchdog& wd) {
+                                          const Watchdog& wd) {
   constexpr int ST = Cfg::STAGES;
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
   const uint32_t sbase = smem_addr(smem);
@@ -205,41 +208,54 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
   tma_prefetch_desc(&p.tm_k);
   tma_prefetch_desc(&p.tm_v);
   tma_prefetch_desc(&p.tm_o);
-
-  mbar_arrive_expect_tx(bar(Cfg::kBarQFull), Cfg::NQ * Cfg::kTileBytes);
-#pragma unroll
-  for (int i = 0; i < Cfg::NQ; ++i) {
-    tma_load_3d(sbase + Cfg::kQOff + i * Cfg::kTileBytes, &p.tm_q, bar(Cfg::kBarQFull), 0,
-                q_row0 + i * Cfg::kRows, head);
-  }
-  // K/V blocks are re-read by every query-tile CTA of this head: keep them in L2.
+  // K/V blocks are re-read by every query-block pass over the same head: keep them in L2.
   const uint64_t keep = l2_policy_evict_last();
-  int issued = 0;
-  for (int j = 0; j < nkb; ++j) {
-    const int st = j % ST;
-    const uint32_t ph = static_cast<uint32_t>(j / ST) & 1u;
+
+  StepCursor cur;
+  cur.init(p);
+  int g = 0;  // global step index of this CTA
+  int q_loaded = 0, k_issued = 0, v_issued = 0;
+  while (cur.valid()) {
+    if (cur.first_step()) {
+      const int s = cur.seg_idx, b = s & 1;
+      if (!wait_single(bar(Cfg::kBarQEmpty + b), (static_cast<uint32_t>(s >> 1) & 1u) ^ 1u, wd,
+                       kSiteLoadQEmpty))
+        break;
+      mbar_arrive_expect_tx(bar(Cfg::kBarQFull + b), Cfg::NQ * Cfg::kTileBytes);
+#pragma unroll
+      for (int i = 0; i < Cfg::NQ; ++i) {
+        tma_load_3d(sbase + Cfg::kQOff + (b * Cfg::NQ + i) * Cfg::kTileBytes, &p.tm_q,
+                    bar(Cfg::kBarQFull + b), 0,
+                    (cur.u % p.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, cur.u / p.q_blocks);
+      }
+      q_loaded = s + 1;
+    }
+    const int st = g % ST;
+    const uint32_t ph = static_cast<uint32_t>(g / ST) & 1u;
     if (!wait_single(bar(Cfg::kBarKEmpty + st), ph ^ 1u, wd, kSiteLoadKEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarKFull + st), Cfg::kTileBytes);
     tma_load_3d_hint(sbase + Cfg::kKOff + st * Cfg::kTileBytes, &p.tm_k, bar(Cfg::kBarKFull + st),
-                     0, j * Cfg::kKeys, head, keep);
-    if (!wait_single(bar(Cfg::kBarVEmpty + st), ph ^ 1u, wd, kSiteLoadVEmpty)) {
-      issued = -(j + 1);  // K of block j issued, V not
-      break;
-    }
+                     0, cur.j * Cfg::kKeys, cur.u / p.q_blocks, keep);
+    k_issued = g + 1;
+    if (!wait_single(bar(Cfg::kBarVEmpty + st), ph ^ 1u, wd, kSiteLoadVEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarVFull + st), Cfg::kTileBytes);
     tma_load_3d_hint(sbase + Cfg::kVOff + st * Cfg::kTileBytes, &p.tm_v, bar(Cfg::kBarVFull + st),
-                     0, j * Cfg::kKeys, head, keep);
-    issued = j + 1;
+                     0, cur.j * Cfg::kKeys, cur.u / p.q_blocks, keep);
+    v_issued = g + 1;
+    ++g;
+    cur.step(p);
   }
   if (*wd.abort) {
     // Unwinding: wait for every copy this thread put in flight before shared memory goes away.
-    drain_wait(bar(Cfg::kBarQFull), 0);
-    const int k_blocks = issued >= 0 ? issued : -issued;
-    const int v_blocks = issued >= 0 ? issued : -issued - 1;
+    for (int b = 0; b < 2; ++b) {
+      int last = -1;
+      for (int s = b; s < q_loaded; s += 2) last = s;
+      if (last >= 0) drain_wait(bar(Cfg::kBarQFull + b), static_cast<uint32_t>(last >> 1) & 1u);
+    }
     for (int st = 0; st < ST; ++st) {
       int last_k = -1, last_v = -1;
-      for (int j = st; j < k_blocks; j += ST) last_k = j;
-      for (int j = st; j < v_blocks; j += ST) last_v = j;
+      for (int x = st; x < k_issued; x += ST) last_k = x;
+      for (int x = st; x < v_issued; x += ST) last_v = x;
       if (last_k >= 0) drain_wait(bar(Cfg::kBarKFull + st), static_cast<uint32_t>(last_k / ST) & 1u);
       if (last_v >= 0) drain_wait(bar(Cfg::kBarVFull + st), static_cast<uint32_t>(last_v / ST) & 1u);
     }
@@ -248,21 +264,22 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
 
 // Executed by the whole MMA warp: waits and descriptor arithmetic stay warp-uniform (uniform
 // datapath, no per-MMA register moves); one elected lane issues tcgen05.mma / commit. Issue
-// cost per MMA matters here: a 128x64x16 P.V step is only 32 tensor-core cycles.
+// cost per MMA matters here: a 128x64x16 P.V step is only 32 tensor-core cycles. S for step
+// g+1 is issued before P.V of step g, so the next scores are computed while the softmax warps
+// still work on the current block (also across unit boundaries).
 template <class Cfg>
 __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint32_t bars,
-                                         uint32_t tmem, int nkb, const Watchdog& wd) {
+                                         uint32_t tmem, const Watchdog& wd) {
   constexpr int ST = Cfg::STAGES;
   constexpr int NQ = Cfg::NQ;
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
   const uint32_t sbase = smem_addr(smem);
   constexpr uint32_t kIdescS = idesc_f16_f32(128, 128, false);
   constexpr uint32_t kIdescO = idesc_f16_f32(128, 64, true);
-  // K-major Q / K tiles: SBO = 1024 (8-row swizzle atoms), LBO unused (16).
-  constexpr uint32_t kHiKMajor = smem_desc_hi(1024, kSwizzle128B);
-  // MN-major V tile (d contiguous): SBO = 1024 between 8-key groups, LBO = one tile (unused,
-  // the 64 d-columns are a single 128-byte swizzle atom).
-  constexpr uint32_t kHiMNMajor = smem_desc_hi(1024, kSwizzle128B);
+  // K-major Q / K tiles: SBO = 1024 (8-row swizzle atoms), LBO unused (16). MN-major V tile
+  // (d contiguous): SBO = 1024 between 8-key groups, LBO = one tile (unused: the 64
+  // d-columns are a single 128-byte swizzle atom).
+  constexpr uint32_t kHi = smem_desc_hi(1024, kSwizzle128B);
   const uint32_t q_lo = smem_desc_lo(sbase + Cfg::kQOff, 16);
   const uint32_t k_lo = smem_desc_lo(sbase + Cfg::kKOff, 16);
   const uint32_t v_lo = smem_desc_lo(sbase + Cfg::kVOff, Cfg::kTileBytes);
@@ -270,65 +287,86 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
   const bool leader = elect_one();
   bool issued_any = false;
 
-  if (!wait_warp(bar(Cfg::kBarQFull), 0, wd, kSiteMmaQ)) goto unwind;
-
-  for (int j = -1; j < nkb; ++j) {
-    // ---- S_i[j+1] = Q_i K_{j+1}^T as soon as softmax_i has pulled S_i[j] into registers.
-    if (j + 1 < nkb) {
-      const int st1 = (j + 1) % ST;
-      const uint32_t ph1 = static_cast<uint32_t>((j + 1) / ST) & 1u;
-      if (!wait_warp(bar(Cfg::kBarKFull + st1), ph1, wd, kSiteMmaK)) goto unwind;
-      const uint32_t kd = k_lo + st1 * kTileStep;
-#pragma unroll
-      for (int i = 0; i < NQ; ++i) {
-        if (j >= 0) {
-          if (!wait_warp(bar(Cfg::kBarSFree + i), static_cast<uint32_t>(j) & 1u, wd,
-                         kSiteMmaSFree))
-            goto unwind;
-        }
-        tc_fence_after();
-        if (leader) {
-          const uint32_t qd = q_lo + i * kTileStep;
-          const uint32_t d_tmem = tmem + Cfg::kColS + 128 * i;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {  // 16 of the 64 head dims per MMA (32 bytes)
-            mma_ss(d_tmem, desc_join(qd + 2 * kk, kHiKMajor), desc_join(kd + 2 * kk, kHiKMajor),
-                   kIdescS, kk > 0 ? 1u : 0u);
-          }
-          mma_commit(bar(Cfg::kBarSFull + i));
-        }
-        __syncwarp();
-        issued_any = true;
-      }
-      if (leader) mma_commit(bar(Cfg::kBarKEmpty + st1));
-      __syncwarp();
+  StepCursor cs, cp;  // next S step, next P.V step
+  cs.init(p);
+  cp.init(p);
+  int gs = 0, gp = 0;
+  // S_i[gs] = Q_i K_gs^T once softmax_i has pulled S_i[gs-1] into registers.
+  auto issue_s = [&]() -> bool {
+    const int b = cs.seg_idx & 1;
+    if (cs.first_step()) {
+      if (!wait_warp(bar(Cfg::kBarQFull + b), static_cast<uint32_t>(cs.seg_idx >> 1) & 1u, wd,
+                     kSiteMmaQ))
+        return false;
     }
-    if (j < 0) continue;
-    // ---- O_i += P_i[j] V_j once softmax_i has written P_i[j] (and rescaled O_i if needed).
-    const int st = j % ST;
-    const uint32_t ph = static_cast<uint32_t>(j / ST) & 1u;
-    if (!wait_warp(bar(Cfg::kBarVFull + st), ph, wd, kSiteMmaV)) goto unwind;
-    const uint32_t vd = v_lo + st * kTileStep;
+    const int st = gs % ST;
+    if (!wait_warp(bar(Cfg::kBarKFull + st), static_cast<uint32_t>(gs / ST) & 1u, wd, kSiteMmaK))
+      return false;
+    const uint32_t kd = k_lo + st * kTileStep;
 #pragma unroll
     for (int i = 0; i < NQ; ++i) {
-      if (!wait_warp(bar(Cfg::kBarPFull + i), static_cast<uint32_t>(j) & 1u, wd, kSiteMmaPFull))
-        goto unwind;
+      if (gs > 0) {
+        if (!wait_warp(bar(Cfg::kBarSFree + i), static_cast<uint32_t>(gs - 1) & 1u, wd,
+                       kSiteMmaSFree))
+          return false;
+      }
       tc_fence_after();
       if (leader) {
-        const uint32_t d_tmem = tmem + Cfg::kColO + 64 * i;
-        const uint32_t a_tmem = tmem + Cfg::kColP + 64 * i;
+        const uint32_t qd = q_lo + (b * NQ + i) * kTileStep;
+        const uint32_t d_tmem = tmem + Cfg::kColS + 128 * i;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: two 8-key swizzle atoms (2 KiB)
-          mma_ts(d_tmem, a_tmem + 8 * kk, desc_join(vd + 128 * kk, kHiMNMajor), kIdescO,
-                 (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {  // 16 of the 64 head dims per MMA (32 bytes)
+          mma_ss(d_tmem, desc_join(qd + 2 * kk, kHi), desc_join(kd + 2 * kk, kHi), kIdescS,
+                 kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(Cfg::kBarODone + i));
+        mma_commit(bar(Cfg::kBarSFull + i));
       }
       __syncwarp();
       issued_any = true;
     }
-    if (leader) mma_commit(bar(Cfg::kBarVEmpty + st));
+    if (leader) mma_commit(bar(Cfg::kBarKEmpty + st));
     __syncwarp();
+    ++gs;
+    cs.step(p);
+    return true;
+  };
+
+  if (cs.valid() && !issue_s()) goto unwind;
+  while (cp.valid()) {
+    // S of the next step goes in before P.V of this one, so the tensor core computes the
+    // next scores while the softmax warps are still busy with this block.
+    if (cs.valid() && !issue_s()) goto unwind;
+    // ---- O_i += P_i[gp] V_gp once softmax_i has written P_i[gp] (and rescaled O_i if needed).
+    {
+      const int st = gp % ST;
+      if (!wait_warp(bar(Cfg::kBarVFull + st), static_cast<uint32_t>(gp / ST) & 1u, wd, kSiteMmaV))
+        goto unwind;
+      const uint32_t vd = v_lo + st * kTileStep;
+      const bool fresh = cp.first_step();  // first block of a unit: overwrite O
+#pragma unroll
+      for (int i = 0; i < NQ; ++i) {
+        if (!wait_warp(bar(Cfg::kBarPFull + i), static_cast<uint32_t>(gp) & 1u, wd,
+                       kSiteMmaPFull))
+          goto unwind;
+        tc_fence_after();
+        if (leader) {
+          const uint32_t d_tmem = tmem + Cfg::kColO + 64 * i;
+          const uint32_t a_tmem = tmem + Cfg::kColP + 64 * i;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: two 8-key swizzle atoms (2 KiB)
+            mma_ts(d_tmem, a_tmem + 8 * kk, desc_join(vd + 128 * kk, kHi), kIdescO,
+                   (!fresh || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar(Cfg::kBarODone + i));
+        }
+        __syncwarp();
+        issued_any = true;
+      }
+      if (leader) mma_commit(bar(Cfg::kBarVEmpty + st));
+      __syncwarp();
+      ++gp;
+      cp.step(p);
+    }
   }
   return;
 
@@ -341,10 +379,135 @@ unwind:
   }
 }
 
+// Maximum of the 64 scores of the other column half of this thread's row, read from TMEM in
+// two 32-column loads; with kMasked, columns at or past `valid` count as -inf.
+template <bool kMasked>
+__device__ __forceinline__ float other_half_max(uint32_t taddr, int valid) {
+  float a = -INFINITY, b = -INFINITY;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t t[32];
+    tmem_ld32_sync(taddr + 32 * h, t);
+    if (kMasked) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (32 * h + k >= valid) t[k] = __float_as_uint(-INFINITY);
+    }
+#pragma unroll
+    for (int k = 0; k < 32; k += 4) {
+      a = max3(a, __uint_as_float(t[k]), __uint_as_float(t[k + 1]));
+      b = max3(b, __uint_as_float(t[k + 2]), __uint_as_float(t[k + 3]));
+    }
+  }
+  return fmaxf(a, b);
+}
+
+// One step of a softmax thread: scores of its row and column half for one key block -> P in
+// TMEM (fp16), running max / sum updated, O rescaled in TMEM when the max was raised.
+// Returns false if the CTA is unwinding.
+template <class Cfg>
+__device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, uint32_t tS,
+                                             uint32_t tS_other, uint32_t tP, uint32_t tO,
+                                             int tile, int half, int lane, int g, int j,
+                                             bool first, float& m_run, float& l_run,
+                                             const Watchdog& wd) {
+  auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
+  const float c = p.scale_log2;
+  if (!wait_warp(bar(Cfg::kBarSFull + tile), static_cast<uint32_t>(g) & 1u, wd, kSiteSoftSFull))
+    return false;
+  tc_fence_after();
+  // The other half of the row is read only for its maximum, 32 columns at a time, so the two
+  // threads of a row never wait for each other inside the loop.
+  const float om = j == p.nkb - 1
+                       ? other_half_max<true>(tS_other, p.n - j * Cfg::kKeys - 64 * (half ^ 1))
+                       : other_half_max<false>(tS_other, 64);
+  uint32_t sr[64];
+  tmem_ld64_sync(tS, sr);
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar(Cfg::kBarSFree + tile));
+
+  if (j == p.nkb - 1) {
+    // last key block of the sequence: columns past N score -inf (both halves)
+    const int valid = p.n - j * Cfg::kKeys - 64 * half;
+#pragma unroll
+    for (int k = 0; k < 64; ++k)
+      if (k >= valid) sr[k] = __float_as_uint(-INFINITY);
+  }
+
+  // Row max: this half (four 3-input max chains: 4 seeds, 7 x 8, 4 tail) and the other half.
+  float mx[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) mx[a] = __uint_as_float(sr[a]);
+#pragma unroll
+  for (int k = 4; k < 60; k += 8) {
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+      mx[a] = max3(mx[a], __uint_as_float(sr[k + 2 * a]), __uint_as_float(sr[k + 2 * a + 1]));
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) mx[a] = fmaxf(mx[a], __uint_as_float(sr[60 + a]));
+  const float m_blk = max3(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]), om) * c;
+  const float m_new = fmaxf(m_run, m_blk);
+  // Raise the reference max only when some row of the warp grew past the threshold. Both
+  // warps of a row see the same scores, so they take the same decision.
+  const bool grow = __any_sync(0xffffffffu, m_new > m_run + Cfg::kRescaleThreshold);
+  const float m_use = grow ? m_new : m_run;
+  const float alpha = ex2_approx(m_run - m_use);  // 0 on a unit's first block (m_run = -inf)
+  const float neg_m = -m_use;
+
+  // Scale-subtract and row sum run on packed pairs (fma/add .f32x2). Pairs whose index has
+  // its bit set in kPolyMask take exp2 from the FMA-pipe polynomial, the others from MUFU.
+  const uint64_t c2 = f2_splat(c);
+  const uint64_t negm2 = f2_splat(neg_m);
+  uint32_t pk[32];
+  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const uint64_t x =
+        f2_fma(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])), c2, negm2);
+    float x0, x1, e0, e1;
+    f2_unpack(x, x0, x1);
+    if ((Cfg::kPolyMask >> (k & 7)) & 1u) {
+      exp2_poly_pair(x0, x1, e0, e1);
+    } else {
+      e0 = ex2_approx(x0);
+      e1 = ex2_approx(x1);
+    }
+    acc[k & 3] = f2_add(acc[k & 3], f2_pack(e0, e1));
+    pk[k] = pack_half2(e0, e1);
+  }
+  float acc0, acc1, acc2, acc3;
+  f2_unpack(f2_add(acc[0], acc[1]), acc0, acc1);
+  f2_unpack(f2_add(acc[2], acc[3]), acc2, acc3);
+  l_run = l_run * alpha + ((acc0 + acc1) + (acc2 + acc3));
+  m_run = m_use;
+
+  // P and O are free once the previous O += P V has completed.
+  if (g > 0) {
+    if (!wait_warp(bar(Cfg::kBarODone + tile), static_cast<uint32_t>(g - 1) & 1u, wd,
+                   kSiteSoftODone))
+      return false;
+    tc_fence_after();
+  }
+  tmem_st32(tP, pk);
+  if (grow && !first) {
+    uint32_t o[32];
+    tmem_ld32_sync(tO, o);
+#pragma unroll
+    for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+    tmem_st32(tO, o);
+  }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar(Cfg::kBarPFull + tile));
+  return true;
+}
+
 template <class Cfg>
 __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, uint32_t bars,
-                                             uint32_t tmem, int tile, int head, int q_row0,
-                                             int nkb, const Watchdog& wd) {
+                                             uint32_t tmem, int tile, const Watchdog& wd) {
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -353,172 +516,101 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   const int row = quad * 32 + lane;       // row of the query tile == TMEM lane
   const uint32_t lane_bits = static_cast<uint32_t>(quad * 32) << 16;
   const uint32_t tS = tmem + lane_bits + Cfg::kColS + 128 * tile + 64 * half;
+  const uint32_t tS_other = tmem + lane_bits + Cfg::kColS + 128 * tile + 64 * (half ^ 1);
   const uint32_t tP = tmem + lane_bits + Cfg::kColP + 64 * tile + 32 * half;
   const uint32_t tO = tmem + lane_bits + Cfg::kColO + 64 * tile + 32 * half;
-  // partner exchange slots: xch[parity][tile][half][row]
-  float* xch = reinterpret_cast<float*>(smem + Cfg::kXchOff);
-  auto slot = [&](int parity, int h) {
-    return xch + ((parity * Cfg::NQ + tile) * 2 + h) * Cfg::kRows + row;
-  };
-  const int pair_bar = 1 + tile * 4 + quad;  // the two warps that share these 32 rows
-  const float c = p.scale_log2;
+  float* xch = reinterpret_cast<float*>(smem + Cfg::kXchOff);  // [tile][half][row] row sums
 
-  float m_run = -INFINITY;  // running max of s*scale*log2(e), identical in both threads
-  float l_run = 0.0f;       // this thread's partial sum of p over its column half
-  bool ok = true;
-  // Tile 1 hands tile 0 the first exp turn.
-  if (Cfg::kPingPong && tile == 1 && lane == 0) mbar_arrive(bar(Cfg::kBarExpTok + 0));
-
-  for (int j = 0; j < nkb; ++j) {
-    if (!wait_warp(bar(Cfg::kBarSFull + tile), static_cast<uint32_t>(j) & 1u, wd, kSiteSoftSFull)) {
-      ok = false;
-      break;
+  int g = 0;       // global step index (phase of the per-step barriers)
+  int stores = 0;  // whole units stored so far (phase of the staging barrier)
+  StepCursor cur;
+  cur.init(p);
+  while (cur.valid()) {
+    float m_run = -INFINITY;  // running max of s*scale*log2(e), identical in both threads
+    float l_run = 0.0f;       // this thread's partial sum of p over its column half
+    for (int j = cur.j0; j < cur.j1; ++j, ++g) {
+      if (!softmax_step<Cfg>(p, bars, tS, tS_other, tP, tO, tile, half, lane, g, j, j == cur.j0,
+                             m_run, l_run, wd))
+        return;
     }
+    // ---- unit epilogue (g - 1 is the unit's last step)
+    if (!wait_warp(bar(Cfg::kBarODone + tile), static_cast<uint32_t>(g - 1) & 1u, wd,
+                   kSiteSoftOFinal))
+      return;
     tc_fence_after();
-    uint32_t sr[64];
-    tmem_ld64_sync(tS, sr);
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar(Cfg::kBarSFree + tile));
-
-    const int valid = p.n - j * Cfg::kKeys - 64 * half;
-    if (valid < 64) {
-#pragma unroll
-      for (int k = 0; k < 64; ++k)
-        if (k >= valid) sr[k] = __float_as_uint(-INFINITY);
-    }
-
-    // Partial max over this half: four 3-input max chains (4 seeds, 7 x 8, 4 tail = 64).
-    float mx[4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a) mx[a] = __uint_as_float(sr[a]);
-#pragma unroll
-    for (int k = 4; k < 60; k += 8) {
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-        mx[a] = max3(mx[a], __uint_as_float(sr[k + 2 * a]), __uint_as_float(sr[k + 2 * a + 1]));
-    }
-#pragma unroll
-    for (int a = 0; a < 4; ++a) mx[a] = fmaxf(mx[a], __uint_as_float(sr[60 + a]));
-    const float pm = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-    // Trade partial maxima with the partner thread (same row, other half). Slots alternate
-    // with the step parity so a partner one step ahead never overwrites an unread value.
-    *slot(j & 1, half) = pm;
-    named_bar_sync(pair_bar, 64);
-    const float m_blk = fmaxf(pm, *slot(j & 1, half ^ 1)) * c;
-    const float m_new = fmaxf(m_run, m_blk);
-    // Raise the reference max only when some row of the warp grew past the threshold. Both
-    // warps of a pair hold the same rows and values, so they take the same decision.
-    const bool grow = __any_sync(0xffffffffu, m_new > m_run + Cfg::kRescaleThreshold);
-    const float m_use = grow ? m_new : m_run;
-    const float alpha = ex2_approx(m_run - m_use);  // 0 on the first block (m_run = -inf)
-    float neg_m = -m_use;
-    if constexpr (Cfg::kPingPong) {
-      if (!wait_warp(bar(Cfg::kBarExpTok + tile), static_cast<uint32_t>(j) & 1u, wd,
-                     kSiteSoftExpTok)) {
-        ok = false;
-        break;
-      }
-      // Pin the exp loop below the token wait: it depends on neg_m "produced" here.
-      asm volatile("" : "+f"(neg_m)::"memory");
-    }
-
-    // Scale-subtract and row sum run on packed pairs (fma/add .f32x2). Pairs whose index
-    // has its bit set in kPolyMask take exp2 from the FMA-pipe polynomial, the others from
-    // MUFU ex2, so both units work on every row.
-    const uint64_t c2 = f2_splat(c);
-    const uint64_t negm2 = f2_splat(neg_m);
-    uint32_t pk[32];
-    uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const uint64_t x =
-          f2_fma(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])), c2, negm2);
-      float x0, x1, e0, e1;
-      f2_unpack(x, x0, x1);
-      if ((Cfg::kPolyMask >> (k & 7)) & 1u) {
-        exp2_poly_pair(x0, x1, e0, e1);
-      } else {
-        e0 = ex2_approx(x0);
-        e1 = ex2_approx(x1);
-      }
-      acc[k & 3] = f2_add(acc[k & 3], f2_pack(e0, e1));
-      pk[k] = pack_half2(e0, e1);
-    }
-    float acc0, acc1, acc2, acc3;
-    f2_unpack(f2_add(acc[0], acc[1]), acc0, acc1);
-    f2_unpack(f2_add(acc[2], acc[3]), acc2, acc3);
-    l_run = l_run * alpha + ((acc0 + acc1) + (acc2 + acc3));
-    m_run = m_use;
-    if constexpr (Cfg::kPingPong) {
-      // Keep the exp results above the hand-over, then pass the turn to the other tile.
-      regs_ready(pk, l_run);
+    // Row sum = both halves' partial sums (the one place the two threads of a row meet).
+    float* my = xch + (tile * 2 + half) * Cfg::kRows + row;
+    float* other = xch + (tile * 2 + (half ^ 1)) * Cfg::kRows + row;
+    *my = l_run;
+    {
+      const int xb = Cfg::kBarXchSum + tile * 4 + quad;
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(Cfg::kBarExpTok + (tile ^ 1)));
+      if (lane == 0) mbar_arrive(bar(xb));
+      if (!wait_warp(bar(xb), static_cast<uint32_t>(cur.seg_idx) & 1u, wd, kSiteSoftXch)) return;
     }
-
-    // P_i and O_i are free once the previous O_i += P_i V has completed.
-    if (j > 0) {
-      if (!wait_warp(bar(Cfg::kBarODone + tile), static_cast<uint32_t>(j - 1) & 1u, wd,
-                     kSiteSoftODone)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-    }
-    tmem_st32(tP, pk);
-    if (grow && j > 0) {
-      uint32_t o[32];
-      tmem_ld32_sync(tO, o);
-#pragma unroll
-      for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-      tmem_st32(tO, o);
-    }
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar(Cfg::kBarPFull + tile));
-  }
-
-  // ---- epilogue: O / l -> fp16 -> swizzled staging (this tile's Q slot) -> TMA store.
-  if (ok) {
-    ok = wait_warp(bar(Cfg::kBarODone + tile), static_cast<uint32_t>(nkb - 1) & 1u, wd,
-                   kSiteSoftOFinal);
-  }
-  // Row sum = both halves' partial sums (every thread reaches this barrier, ok or not).
-  *slot(nkb & 1, half) = l_run;
-  named_bar_sync(pair_bar, 64);
-  const float l_row = l_run + *slot(nkb & 1, half ^ 1);
-  uint8_t* stage = smem + Cfg::kQOff + tile * Cfg::kTileBytes;
-  if (ok) {
-    tc_fence_after();
-    const float inv_l = 1.0f / l_row;
+    const float l_row = l_run + *other;
     uint32_t o[32];
     tmem_ld32_sync(tO, o);
+    tc_fence_before();
+    const int b = cur.seg_idx & 1;
+    if (cur.whole(p.nkb)) {
+      // O / l -> fp16 -> swizzled staging (this tile's slot of the unit's Q buffer) -> TMA.
+      uint8_t* stage = smem + Cfg::kQOff + (b * Cfg::NQ + tile) * Cfg::kTileBytes;
+      const float inv_l = 1.0f / l_row;
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {  // 4 chunks of 8 halves = 16 bytes each
-      uint32_t w[4];
+      for (int ch = 0; ch < 4; ++ch) {  // 4 chunks of 8 halves = 16 bytes each
+        uint32_t w[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        w[e] = pack_half2(__uint_as_float(o[8 * ch + 2 * e]) * inv_l,
-                          __uint_as_float(o[8 * ch + 2 * e + 1]) * inv_l);
+        for (int e = 0; e < 4; ++e) {
+          w[e] = pack_half2(__uint_as_float(o[8 * ch + 2 * e]) * inv_l,
+                            __uint_as_float(o[8 * ch + 2 * e + 1]) * inv_l);
+        }
+        const int chunk = 4 * half + ch;
+        const uint32_t dst = smem_addr(stage + row * 128 + ((chunk ^ (row & 7)) << 4));
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]),
+                     "r"(w[1]), "r"(w[2]), "r"(w[3])
+                     : "memory");
       }
-      const int chunk = 4 * half + ch;
-      const uint32_t dst = smem_addr(stage + row * 128 + ((chunk ^ (row & 7)) << 4));
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]), "r"(w[1]),
-                   "r"(w[2]), "r"(w[3])
-                   : "memory");
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(Cfg::kBarStage + tile));
+      if (half == 0 && row == 0) {
+        // the tile's eight warps have written their staging rows: store, then free the
+        // Q buffer once the store has read it
+        if (!wait_single(bar(Cfg::kBarStage + tile), static_cast<uint32_t>(stores) & 1u, wd,
+                         kSiteSoftStage))
+          return;
+        const int r0 = (cur.u % p.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
+        if (r0 < p.n) {
+          tma_store_3d(&p.tm_o, smem_addr(stage), 0, r0, cur.u / p.q_blocks);
+          tma_store_commit();
+          tma_store_wait_read();
+        }
+        mbar_arrive(bar(Cfg::kBarQEmpty + b));
+      }
+      ++stores;
+    } else {
+      // A piece of a query block: unnormalised O, the row max and the row sum go to this
+      // CTA's workspace slot (first or last segment of its range) for the merge kernel.
+      float* ws = p.workspace +
+                  static_cast<size_t>(2 * blockIdx.x + (cur.first_of_range() ? 0 : 1)) *
+                      Cfg::kSlotFloats;
+      const int r = tile * Cfg::kRows + row;
+      float4* dst =
+          reinterpret_cast<float4*>(ws + static_cast<size_t>(r) * Cfg::kHeadDim + 32 * half);
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4) {
+        dst[q4] = make_float4(__uint_as_float(o[4 * q4]), __uint_as_float(o[4 * q4 + 1]),
+                              __uint_as_float(o[4 * q4 + 2]), __uint_as_float(o[4 * q4 + 3]));
+      }
+      if (half == 0) {
+        ws[Cfg::kRowsPerUnit * Cfg::kHeadDim + r] = m_run;
+        ws[Cfg::kRowsPerUnit * (Cfg::kHeadDim + 1) + r] = l_row;
+      }
+      // the Q buffer was only read by this unit's S MMAs, all complete by now
+      if (half == 0 && row == 0) mbar_arrive(bar(Cfg::kBarQEmpty + b));
     }
-    fence_proxy_async_smem();
-  }
-  named_bar_sync(9 + tile, 256);
-  if (ok && half == 0 && row == 0 && !*wd.abort) {
-    const int r0 = q_row0 + tile * Cfg::kRows;
-    if (r0 < p.n) {
-      tma_store_3d(&p.tm_o, smem_addr(stage), 0, r0, head);
-      tma_store_commit();
-      tma_store_wait_read();
-    }
+    cur.next_segment(p);
   }
 }
 
@@ -531,10 +623,6 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int head = static_cast<int>(blockIdx.x) / p.q_blocks;
-  const int q_block = static_cast<int>(blockIdx.x) % p.q_blocks;
-  const int q_row0 = q_block * Cfg::kRows * NQ;
-  const int nkb = (p.n + Cfg::kKeys - 1) / Cfg::kKeys;
 
   const uint32_t bars = smem_addr(smem + Cfg::kBarOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kTmemSlotOff);
@@ -542,7 +630,10 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    mbar_init(bars + 8 * Cfg::kBarQFull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bars + 8 * (Cfg::kBarQFull + b), 1);
+      mbar_init(bars + 8 * (Cfg::kBarQEmpty + b), Cfg::NQ);  // one arrive per tile epilogue
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bars + 8 * (Cfg::kBarKFull + s), 1);
       mbar_init(bars + 8 * (Cfg::kBarKEmpty + s), 1);
@@ -555,8 +646,8 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
       mbar_init(bars + 8 * (Cfg::kBarPFull + i), 8);
       mbar_init(bars + 8 * (Cfg::kBarODone + i), 1);
     }
-    mbar_init(bars + 8 * (Cfg::kBarExpTok + 0), 8);
-    mbar_init(bars + 8 * (Cfg::kBarExpTok + 1), 8);
+    for (int x = 0; x < NQ * 4; ++x) mbar_init(bars + 8 * (Cfg::kBarXchSum + x), 2);
+    for (int i = 0; i < NQ; ++i) mbar_init(bars + 8 * (Cfg::kBarStage + i), 8);
     mbar_init(bars + 8 * Cfg::kBarDrain, 1);
     mbar_init_fence();
   }
@@ -573,19 +664,90 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
   if (warp >= Cfg::kSoftmaxWarps) {
     if constexpr (Cfg::kRebalanceRegs) setmaxnreg_dec<Cfg::kControlRegs>();
     if (warp == Cfg::kLoadWarp) {
-      if (lane == 0) load_role<Cfg>(p, smem, bars, head, q_row0, nkb, wd);
+      if (lane == 0) load_role<Cfg>(p, smem, bars, wd);
     } else if (warp == Cfg::kMmaWarp) {
-      mma_role<Cfg>(p, smem, bars, tmem, nkb, wd);
+      mma_role<Cfg>(p, smem, bars, tmem, wd);
     }
   } else {
     if constexpr (Cfg::kRebalanceRegs) setmaxnreg_inc<Cfg::kSoftmaxRegs>();
-    softmax_role<Cfg>(p, smem, bars, tmem, warp / 8, head, q_row0, nkb, wd);
+    softmax_role<Cfg>(p, smem, bars, tmem, warp / 8, wd);
   }
   __syncwarp();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+}
+
+// ---------------------------------------------------------------- split-mode merge
+struct MergeParams {
+  void* out;          // fp16 [BH][N][64]
+  const float* workspace;
+  int n, bh, q_blocks, nkb;
+  int ctas;           // grid size of the forward kernel whose pieces are merged
+};
+
+// One CTA per forward CTA c; it merges the query block that starts inside c's range and
+// continues past it (if any): every piece's O is rescaled to the common row max, summed,
+// divided by the rescaled sum of row sums, rounded to fp16. One thread per query row.
+template <int kRowsPerUnit, int kSlotFloats>
+__global__ void __launch_bounds__(kRowsPerUnit) mfa_merge_kernel(const MergeParams mp) {
+  constexpr int kD = 64;
+  const int c = static_cast<int>(blockIdx.x);
+  const long long units = static_cast<long long>(mp.bh) * mp.q_blocks;
+  long long b0, b1;
+  cta_range(units, mp.nkb, 1, c, mp.ctas, b0, b1);
+  if (b1 <= b0) return;
+  const long long u = (b1 - 1) / mp.nkb;  // query block holding c's last key block
+  if ((u + 1) * mp.nkb <= b1) return;     // it ends inside c: not split here
+  if (u * mp.nkb < b0) return;            // it started in an earlier CTA: merged there
+  const int r = static_cast<int>(threadIdx.x);
+  // Pieces: c's last segment (its first too if c's range starts exactly at u), then the
+  // first segment of every following CTA that overlaps u.
+  auto piece = [&](int cc) {
+    const int slot = cc == c ? (b0 == u * mp.nkb ? 0 : 1) : 0;
+    return mp.workspace + static_cast<size_t>(2 * cc + slot) * kSlotFloats;
+  };
+  auto overlaps = [&](int cc) {
+    long long s0, s1;
+    cta_range(units, mp.nkb, 1, cc, mp.ctas, s0, s1);
+    return cc < mp.ctas && s0 < (u + 1) * mp.nkb;
+  };
+  float m_max = -INFINITY;
+  for (int cc = c; overlaps(cc); ++cc) m_max = fmaxf(m_max, piece(cc)[kRowsPerUnit * kD + r]);
+  float acc[kD];
+#pragma unroll
+  for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
+  float l = 0.0f;
+  for (int cc = c; overlaps(cc); ++cc) {
+    const float* ws = piece(cc);
+    const float w = ex2_approx(ws[kRowsPerUnit * kD + r] - m_max);
+    l += w * ws[kRowsPerUnit * (kD + 1) + r];
+    const float4* o = reinterpret_cast<const float4*>(ws + static_cast<size_t>(r) * kD);
+#pragma unroll
+    for (int q4 = 0; q4 < kD / 4; ++q4) {
+      const float4 v = o[q4];
+      acc[4 * q4] += w * v.x;
+      acc[4 * q4 + 1] += w * v.y;
+      acc[4 * q4 + 2] += w * v.z;
+      acc[4 * q4 + 3] += w * v.w;
+    }
+  }
+  const int head = static_cast<int>(u / mp.q_blocks);
+  const int qrow = static_cast<int>(u % mp.q_blocks) * kRowsPerUnit + r;
+  if (qrow >= mp.n) return;
+  const float inv_l = 1.0f / l;
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(mp.out) +
+                                        (static_cast<size_t>(head) * mp.n + qrow) * kD);
+#pragma unroll
+  for (int q8 = 0; q8 < kD / 8; ++q8) {
+    uint4 w;
+    w.x = pack_half2(acc[8 * q8] * inv_l, acc[8 * q8 + 1] * inv_l);
+    w.y = pack_half2(acc[8 * q8 + 2] * inv_l, acc[8 * q8 + 3] * inv_l);
+    w.z = pack_half2(acc[8 * q8 + 4] * inv_l, acc[8 * q8 + 5] * inv_l);
+    w.w = pack_half2(acc[8 * q8 + 6] * inv_l, acc[8 * q8 + 7] * inv_l);
+    dst[q8] = w;
+  }
 }
 
 }  // namespace mfa

@@ -39,3 +39,54 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = Fa
 
 def forward_wmma(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False) -> torch.Tensor:
     return _load_extension().forward_wmma(q, k, v, causal)
+
+
+def forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                   out: torch.Tensor | None = None, chunks: int = 4,
+                   device: torch.device | int | None = None) -> torch.Tensor:
+    """Attention forward on host tensors: fp16 q, k, v in (preferably pinned) CPU memory,
+    result written to a host tensor (``out`` or a new pinned one).
+
+    The batch*head rows are cut into ``chunks`` pieces that move through three CUDA streams:
+    piece i+1 is copied in while piece i is computed by ``forward`` and piece i-1 is copied
+    back, so the host<->device transfers overlap the kernels. Synchronous: returns when the
+    result is in ``out``. Same shape / dtype / error contract as ``forward``.
+    """
+    if q.is_cuda or k.is_cuda or v.is_cuda:
+        raise RuntimeError("forward_pinned expects host tensors; use forward for CUDA tensors")
+    if not (q.shape == k.shape == v.shape):
+        raise RuntimeError("k must have the same shape as q")
+    if q.dim() not in (3, 4):
+        raise RuntimeError("q must have shape [B, H, N, D]")
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    n, d = q.shape[-2], q.shape[-1]
+    bh = q.numel() // (n * d) if n * d else 0
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    if bh == 0 or n == 0:
+        return out
+    q3, k3, v3, o3 = (x.reshape(bh, n, d) for x in (q, k, v, out))
+    chunks = max(1, min(chunks, bh))
+    bounds = [bh * i // chunks for i in range(chunks + 1)]
+    with torch.cuda.device(dev):
+        s_in, s_run, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        dq, dk, dv, do = (torch.empty((bh, n, d), dtype=q.dtype, device=dev) for _ in range(4))
+        ev_in = [torch.cuda.Event() for _ in range(chunks)]
+        ev_run = [torch.cuda.Event() for _ in range(chunks)]
+        ext = _load_extension()
+        for i in range(chunks):
+            a, b = bounds[i], bounds[i + 1]
+            with torch.cuda.stream(s_in):
+                for src, dst in ((q3, dq), (k3, dk), (v3, dv)):
+                    dst[a:b].copy_(src[a:b], non_blocking=True)
+                ev_in[i].record(s_in)
+            with torch.cuda.stream(s_run):
+                s_run.wait_event(ev_in[i])
+                ext.forward_into(dq[a:b], dk[a:b], dv[a:b], do[a:b], causal)
+                ev_run[i].record(s_run)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_run[i])
+                o3[a:b].copy_(do[a:b], non_blocking=True)
+        s_out.synchronize()  # every stream's work on the device buffers is done here
+    return out

@@ -223,3 +223,24 @@ def test_full_size_config_sampled_rows(name):
     out_simple = mfa.forward_wmma(q, k, v)
     torch.testing.assert_close(out_simple[heads][:, rows].float(), exact, atol=ATOL_NAIVE,
                                rtol=RTOL_NAIVE)
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_forward_pinned_matches_forward(chunks):
+    q, k, v = (randn_cuda((2, 4, 1024, 64), 90 + i) for i in range(3))
+    want = mfa.forward(q, k, v).cpu()
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    got = mfa.forward_pinned(hq, hk, hv, chunks=chunks)
+    assert not got.is_cuda
+    # chunks change B*H per launch and so the work split: same math, different summation order
+    torch.testing.assert_close(got, want, atol=1e-3, rtol=1e-3)
+    out = torch.empty_like(hq)
+    mfa.forward_pinned(hq.reshape(8, 1024, 64), hk.reshape(8, 1024, 64), hv.reshape(8, 1024, 64),
+                       out=out.reshape(8, 1024, 64), chunks=chunks)
+    torch.testing.assert_close(out, want, atol=1e-3, rtol=1e-3)
+
+
+def test_forward_pinned_rejects_device_tensors():
+    q = torch.zeros(1, 1, 128, 64, device="cuda", dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="host tensors"):
+        mfa.forward_pinned(q, q, q)
