@@ -57,6 +57,35 @@ MFA_API int mfa_fwd_f16(const void* q, const void* k, const void* v, void* out, 
 MFA_API int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, void* out, int64_t bh,
                        int64_t n, int32_t d, float scale, int32_t causal, void* stream);
 
+/* Size of the static device scratch array used by mfa_fwd_f16_noalloc (20 MiB). */
+#define MFA_NOALLOC_SCRATCH_BYTES 20971520u
+
+/*
+ * Allocation-free variant of mfa_fwd_f16: same kernels, arguments, checks, messages and
+ * results, but it calls no cudaMalloc / cudaFree / stream-ordered or library allocator.
+ * No counterpart in the reference (whose launchers need no scratch at all).
+ *
+ * For callers that cannot allocate device memory on this path: an engine or framework that
+ * reserves the device's memory for its own allocator at start-up (a further allocation may
+ * fail or fragment its pool), and code that must not enter the CUDA allocator in the middle
+ * of a step (an allocation there can block or fail at a point the caller cannot recover from).
+ *
+ * When B*H*(N/256) does not fill the GPU evenly, the key dimension is split and partial
+ * results are merged; mfa_fwd_f16 takes that scratch from a stream-ordered pool, this entry
+ * point from one file-scope device array of MFA_NOALLOC_SCRATCH_BYTES in the library's device
+ * image (2 x 67,584 bytes per CTA: enough for up to 155 SMs; a B200 has 148). A launch that
+ * would need more returns MFA_ERR_INVALID_ARGUMENT with the required size in the message.
+ *   - Nothing in the scratch has to start at zero: every part a call reads, it first writes.
+ *   - The array is shared by every call on a device: calls that overlap on the GPU (issued
+ *     on different streams without ordering between them) race on it and may return wrong
+ *     results. Serialise them, e.g. by issuing them on one stream.
+ *   - The first call on each device runs its one-time set-up (device checks, kernel
+ *     attributes, cudaGetSymbolAddress of the scratch); make that first call before any
+ *     stream capture.
+ */
+MFA_API int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, void* out, int64_t bh,
+                        int64_t n, int32_t d, float scale, int32_t causal, void* stream);
+
 /* Message of the last failing call made by this thread ("" if none). Replaces the
  * std::runtime_error text of the reference launchers and check_cuda
  * (src/mini_flash_attention/utils.cuh:15-21). */

@@ -233,6 +233,138 @@ int check_common(const void* q, const void* k, const void* v, void* out, int64_t
   return MFA_OK;
 }
 
+}  // namespace
+}  // namespace mfa
+
+// ------------------------------------------------------------------ allocation-free entry
+// Scratch of mfa_fwd_f16_noalloc, part of the library's device image: the split plan's partial
+// results, two slots of 256 query rows x (64 + 2) floats (67,584 bytes each) per forward CTA,
+// so 20 MiB covers up to 155 CTAs; a B200 launches at most 148. Shared by every call on a device.
+static __device__ __align__(256) float g_noalloc_scratch[MFA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace mfa {
+namespace {
+
+struct NoAllocState {
+  std::once_flag once;
+  int error = MFA_OK;
+  std::string message;
+  int* status_ptr = nullptr;
+  float* scratch = nullptr;
+  int num_sms = 0;
+};
+NoAllocState g_noalloc[kMaxDevices];
+
+// One-time per-device set-up of the allocation-free entry point, run with `dev` current: the
+// architecture check and kernel attribute of prepare_device, plus the device addresses of the
+// status word and of the static scratch. It creates no memory pool and allocates nothing.
+int prepare_noalloc(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(MFA_ERR_DEVICE, "device index out of range");
+  NoAllocState& st = g_noalloc[dev];
+  std::call_once(st.once, [&st, dev] {
+    int major = 0, minor = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e == cudaSuccess && (major != 10 || minor != 0)) {
+      st.error = MFA_ERR_DEVICE;
+      st.message = "mini_flash_attention_b200 kernels are built for sm_100a only; device " +
+                   std::to_string(dev) + " is sm_" + std::to_string(major) + std::to_string(minor);
+      return;
+    }
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(mfa_fwd_kernel<FullKernel::NQ, FullKernel::STAGES>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, FullKernel::kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status_ptr), g_device_status);
+    if (e == cudaSuccess)
+      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.scratch), g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      st.error = MFA_ERR_CUDA;
+      st.message = std::string("CUDA error: ") + cudaGetErrorString(e) + " (no-alloc set-up)";
+    }
+  });
+  if (st.error != MFA_OK) return fail(st.error, st.message);
+  return MFA_OK;
+}
+
+// launch_forward's plan (CTA count, split decision) with the split workspace taken from the
+// static scratch instead of a stream-ordered allocation.
+int launch_forward_noalloc(const void* q, const void* k, const void* v, void* out, int64_t bh,
+                           int64_t n, float scale, cudaStream_t stream) {
+  using Cfg = FullKernel;
+  if (bh == 0 || n == 0) return MFA_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  int rc = prepare_noalloc(dev);
+  if (rc != MFA_OK) return rc;
+  const NoAllocState& st = g_noalloc[dev];
+
+  FwdParams p;
+  if ((rc = encode_bhnd(&p.tm_q, q, n, bh)) != MFA_OK) return rc;
+  if ((rc = encode_bhnd(&p.tm_k, k, n, bh)) != MFA_OK) return rc;
+  if ((rc = encode_bhnd(&p.tm_v, v, n, bh)) != MFA_OK) return rc;
+  if ((rc = encode_bhnd(&p.tm_o, out, n, bh)) != MFA_OK) return rc;
+  const int64_t q_blocks = (n + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
+  const int64_t nkb = (n + Cfg::kKeys - 1) / Cfg::kKeys;
+  const int64_t units = q_blocks * bh;
+  if (units > (int64_t(1) << 40) / nkb)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  const int64_t sms = st.num_sms;
+  if (units > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  int64_t ctas = units < sms ? units : sms;
+  int split = 0;
+  if (units % sms != 0 && units < 32 * sms) {
+    const double waves = static_cast<double>(units) / sms;
+    const double busy = waves / static_cast<double>((units + sms - 1) / sms);
+    if (busy < 0.97) {
+      split = 1;
+      ctas = units * nkb < sms ? units * nkb : sms;
+    }
+  }
+  if ((split ? units * nkb / ctas : (units + ctas - 1) / ctas * nkb) >= 0x7fffffffLL)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  p.n = static_cast<int>(n);
+  p.bh = static_cast<int>(bh);
+  p.q_blocks = static_cast<int>(q_blocks);
+  p.nkb = static_cast<int>(nkb);
+  p.split = split;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.timeout_ns = g_watchdog_ns;
+  p.status = st.status_ptr;
+  p.workspace = nullptr;
+  if (split) {
+    // Every slot the merge kernel reads is written by the forward kernel of the same call, so
+    // nothing in the scratch has to start at zero.
+    const size_t bytes = static_cast<size_t>(2 * ctas) * Cfg::kSlotFloats * sizeof(float);
+    if (bytes > MFA_NOALLOC_SCRATCH_BYTES)
+      return fail(MFA_ERR_INVALID_ARGUMENT,
+                  "mfa_fwd_f16_noalloc: this launch needs " + std::to_string(bytes) +
+                      " bytes of scratch, more than its static " +
+                      std::to_string(MFA_NOALLOC_SCRATCH_BYTES) + "-byte array");
+    p.workspace = st.scratch;
+  }
+  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES>
+      <<<static_cast<unsigned>(ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  e = cudaGetLastError();
+  if (e == cudaSuccess && split) {
+    MergeParams mp;
+    mp.out = out;
+    mp.workspace = p.workspace;
+    mp.n = p.n;
+    mp.bh = p.bh;
+    mp.q_blocks = p.q_blocks;
+    mp.nkb = p.nkb;
+    mp.ctas = static_cast<int>(ctas);
+    mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats>
+        <<<static_cast<unsigned>(ctas), Cfg::kRowsPerUnit, 0, stream>>>(mp);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
+  return MFA_OK;
+}
+
 // ------------------------------------------------------------------ watchdog self-test
 __device__ int g_selftest_status = 0;
 
@@ -291,6 +423,18 @@ extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, v
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
   return launch_forward<SimpleKernel>(q, k, v, out, bh, n, scale,
                                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, void* out,
+                                   int64_t bh, int64_t n, int32_t d, float scale, int32_t causal,
+                                   void* stream) {
+  int rc = check_common(q, k, v, out, bh, n, d);
+  if (rc != MFA_OK) return rc;
+  if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
+  if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
+  if (causal) return fail(MFA_ERR_CAUSAL, "Causal attention is not supported yet");
+  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  return launch_forward_noalloc(q, k, v, out, bh, n, scale, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" const char* mfa_last_error_string(void) { return g_last_error.c_str(); }

@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libmfa_b200.so"
 EXPORTED_SYMBOLS = (
     "mfa_fwd_f16",
     "mfa_fwd_simple_f16",
+    "mfa_fwd_f16_noalloc",
     "mfa_last_error_string",
     "mfa_device_status",
     "mfa_set_watchdog_ns",
@@ -29,6 +30,7 @@ MFA_ERR_CAUSAL = 4
 MFA_ERR_CUDA = 5
 MFA_ERR_DEVICE = 6
 STATUS_TIMEOUT_BASE = 0x100
+NOALLOC_SCRATCH_BYTES = 20971520  # MFA_NOALLOC_SCRATCH_BYTES
 
 _LIB: ctypes.CDLL | None = None
 
@@ -48,7 +50,7 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
     fwd_args = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                 ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_int32,
                 ctypes.c_void_p]
-    for name in ("mfa_fwd_f16", "mfa_fwd_simple_f16"):
+    for name in ("mfa_fwd_f16", "mfa_fwd_simple_f16", "mfa_fwd_f16_noalloc"):
         fn = getattr(lib, name)
         fn.argtypes = fwd_args
         fn.restype = ctypes.c_int
@@ -83,6 +85,14 @@ def fwd(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, bh: int, n: int, d: in
     lib = load()
     fn = lib.mfa_fwd_simple_f16 if simple else lib.mfa_fwd_f16
     _check(fn(q_ptr, k_ptr, v_ptr, out_ptr, bh, n, d, scale, int(causal), stream))
+
+
+def fwd_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, bh: int, n: int, d: int,
+                scale: float, causal: bool = False, stream: int = 0) -> None:
+    """Launch mfa_fwd_f16_noalloc (no device allocation; static scratch shared by all calls
+    on a device, so calls must not overlap on the GPU); raises MfaError."""
+    _check(load().mfa_fwd_f16_noalloc(q_ptr, k_ptr, v_ptr, out_ptr, bh, n, d, scale,
+                                       int(causal), stream))
 
 
 def device_status(device: int = 0, reset: bool = True) -> int:
