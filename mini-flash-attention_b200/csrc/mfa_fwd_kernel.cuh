@@ -12,10 +12,10 @@
 //
 // B200 structure (not a translation of the mma.sync kernel):
 //   warps 0..8*NQ-1 : softmax warps. Query tile i is owned by warps 8i..8i+7; warp w reads
-//                     TMEM lane quadrant w%4 (32 rows, one row per thread) and column half
-//                     (w/4)%2 of the tile's 128 scores, so two threads share a row: they trade
-//                     their partial row max through shared memory each step and keep partial
-//                     row sums that are combined once, in the epilogue.
+//                     16 rows of TMEM lane quadrant w%4 (upper or lower half by (w/4)%2) as
+//                     16x256b fragments: four neighbouring lanes share a row, two of every
+//                     eight columns each, so row maxima and sums are warp shuffles and the
+//                     softmax warps never wait for one another.
 //   warp  8*NQ      : MMA issuer (whole warp, one elected lane issues): S_i = Q_i K^T (SS
 //                     form) and O_i += P_i V (TS form: P straight from TMEM, V consumed
 //                     MN-major, so no transpose).
@@ -80,16 +80,10 @@ struct FwdConfig {
   static constexpr int kBarSFree = kBarSFull + NQ;
   static constexpr int kBarPFull = kBarSFree + NQ;
   static constexpr int kBarODone = kBarPFull + NQ;
-  // Row-sum exchange between the two warps of a lane quadrant at the end of a unit (count 2,
-  // [tile][quad]); an mbarrier rather than a named barrier, so the wait stays bounded.
-  static constexpr int kBarXchSum = kBarODone + NQ;
-  static constexpr int kBarStage = kBarXchSum + NQ * 4;  // [tile]: output staging written
+  static constexpr int kBarStage = kBarODone + NQ;  // [tile]: output staging written
   static constexpr int kBarDrain = kBarStage + NQ;
   static constexpr int kNumBars = kBarDrain + 1;
-  // partner exchange of the final row sums: [tile][column half][row] floats
-  static constexpr int kXchOff = kBarOff + kNumBars * 8;
-  static constexpr int kXchBytes = NQ * 2 * kRows * 4;
-  static constexpr int kTmemSlotOff = kXchOff + kXchBytes;
+  static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kSmemUsed = kAbortOff + 4;
   static constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for manual 1024 alignment
@@ -379,93 +373,87 @@ unwind:
   }
 }
 
-// Maximum of the 64 scores of the other column half of this thread's row, read from TMEM in
-// two 32-column loads; with kMasked, columns at or past `valid` count as -inf.
-template <bool kMasked>
-__device__ __forceinline__ float other_half_max(uint32_t taddr, int valid) {
-  float a = -INFINITY, b = -INFINITY;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t t[32];
-    tmem_ld32_sync(taddr + 32 * h, t);
-    if (kMasked) {
-#pragma unroll
-      for (int k = 0; k < 32; ++k)
-        if (32 * h + k >= valid) t[k] = __float_as_uint(-INFINITY);
-    }
-#pragma unroll
-    for (int k = 0; k < 32; k += 4) {
-      a = max3(a, __uint_as_float(t[k]), __uint_as_float(t[k + 1]));
-      b = max3(b, __uint_as_float(t[k + 2]), __uint_as_float(t[k + 3]));
-    }
-  }
-  return fmaxf(a, b);
-}
-
-// One step of a softmax thread: scores of its row and column half for one key block -> P in
-// TMEM (fp16), running max / sum updated, O rescaled in TMEM when the max was raised.
-// Returns false if the CTA is unwinding.
+// One step of a softmax warp: the scores of its 16-row slice of a query tile for one key
+// block -> P in TMEM (fp16), running max / sum updated, O rescaled in TMEM when the max was
+// raised. Fragments are TMEM 16x256b: lane 4g + q holds rows g and g + 8 of the slice and,
+// of every group of 8 key columns, columns 2q and 2q + 1; the four threads of a row are
+// neighbouring lanes of one warp, so a row reduction is two shuffles and no two warps ever
+// wait for each other. Returns false if the CTA is unwinding.
 template <class Cfg>
 __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, uint32_t tS,
-                                             uint32_t tS_other, uint32_t tP, uint32_t tO,
-                                             int tile, int half, int lane, int g, int j,
-                                             bool first, float& m_run, float& l_run,
-                                             const Watchdog& wd) {
+                                             uint32_t tP, uint32_t tO, int tile, int lane, int g,
+                                             int j, bool first, float (&m_run)[2],
+                                             float (&l_run)[2], const Watchdog& wd) {
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
+  auto f = [](uint32_t u) { return __uint_as_float(u); };
   const float c = p.scale_log2;
   if (!wait_warp(bar(Cfg::kBarSFull + tile), static_cast<uint32_t>(g) & 1u, wd, kSiteSoftSFull))
     return false;
   tc_fence_after();
-  // The other half of the row is read only for its maximum, 32 columns at a time, so the two
-  // threads of a row never wait for each other inside the loop.
-  const float om = j == p.nkb - 1
-                       ? other_half_max<true>(tS_other, p.n - j * Cfg::kKeys - 64 * (half ^ 1))
-                       : other_half_max<false>(tS_other, 64);
-  uint32_t sr[64];
-  tmem_ld64_sync(tS, sr);
+  uint32_t sr[64];  // sr[4i + e]: row g + 8 (e / 2), key 8i + 2q + e % 2
+  tmem_ld_16x256b_x16_sync(tS, sr);
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(bar(Cfg::kBarSFree + tile));
 
   if (j == p.nkb - 1) {
-    // last key block of the sequence: columns past N score -inf (both halves)
-    const int valid = p.n - j * Cfg::kKeys - 64 * half;
+    // last key block of the sequence: keys past N score -inf
+    const int valid = p.n - j * Cfg::kKeys;
+    if (valid < Cfg::kKeys) {
+      const int q2 = 2 * (lane & 3);
 #pragma unroll
-    for (int k = 0; k < 64; ++k)
-      if (k >= valid) sr[k] = __float_as_uint(-INFINITY);
+      for (int i = 0; i < 16; ++i) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (8 * i + q2 + (e & 1) >= valid) sr[4 * i + e] = __float_as_uint(-INFINITY);
+      }
+    }
   }
 
-  // Row max: this half (four 3-input max chains: 4 seeds, 7 x 8, 4 tail) and the other half.
-  float mx[4];
+  // Row maxima: two 3-input max chains per row over this thread's 32 scores, then the row's
+  // four threads combine theirs.
+  float mrow[2];
 #pragma unroll
-  for (int a = 0; a < 4; ++a) mx[a] = __uint_as_float(sr[a]);
+  for (int r = 0; r < 2; ++r) {
+    float a = fmaxf(f(sr[2 * r]), f(sr[2 * r + 1]));
+    float b = fmaxf(f(sr[4 + 2 * r]), f(sr[5 + 2 * r]));
 #pragma unroll
-  for (int k = 4; k < 60; k += 8) {
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-      mx[a] = max3(mx[a], __uint_as_float(sr[k + 2 * a]), __uint_as_float(sr[k + 2 * a + 1]));
+    for (int i = 2; i < 16; i += 2) {
+      a = max3(a, f(sr[4 * i + 2 * r]), f(sr[4 * i + 2 * r + 1]));
+      b = max3(b, f(sr[4 * i + 4 + 2 * r]), f(sr[4 * i + 5 + 2 * r]));
+    }
+    mrow[r] = fmaxf(a, b);
   }
 #pragma unroll
-  for (int a = 0; a < 4; ++a) mx[a] = fmaxf(mx[a], __uint_as_float(sr[60 + a]));
-  const float m_blk = max3(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]), om) * c;
-  const float m_new = fmaxf(m_run, m_blk);
-  // Raise the reference max only when some row of the warp grew past the threshold. Both
-  // warps of a row see the same scores, so they take the same decision.
-  const bool grow = __any_sync(0xffffffffu, m_new > m_run + Cfg::kRescaleThreshold);
-  const float m_use = grow ? m_new : m_run;
-  const float alpha = ex2_approx(m_run - m_use);  // 0 on a unit's first block (m_run = -inf)
-  const float neg_m = -m_use;
+  for (int r = 0; r < 2; ++r) mrow[r] = fmaxf(mrow[r], __shfl_xor_sync(0xffffffffu, mrow[r], 1));
+#pragma unroll
+  for (int r = 0; r < 2; ++r) mrow[r] = fmaxf(mrow[r], __shfl_xor_sync(0xffffffffu, mrow[r], 2));
+  float m_new[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) m_new[r] = fmaxf(m_run[r], mrow[r] * c);
+  // Raise the reference max only when some row of the warp grew past the threshold; the
+  // four threads of a row hold the same maxima, so they take the same decision.
+  const bool grow = __any_sync(0xffffffffu, m_new[0] > m_run[0] + Cfg::kRescaleThreshold ||
+                                                m_new[1] > m_run[1] + Cfg::kRescaleThreshold);
+  float alpha[2];
+  uint64_t negm2[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const float m_use = grow ? m_new[r] : m_run[r];
+    alpha[r] = ex2_approx(m_run[r] - m_use);  // 0 on a unit's first block (m_run = -inf)
+    m_run[r] = m_use;
+    negm2[r] = f2_splat(-m_use);
+  }
 
-  // Scale-subtract and row sum run on packed pairs (fma/add .f32x2). Pairs whose index has
-  // its bit set in kPolyMask take exp2 from the FMA-pipe polynomial, the others from MUFU.
+  // Scale-subtract and row sums run on packed pairs (fma/add .f32x2); pair k is row k % 2.
+  // Pairs whose index has its bit set in kPolyMask take exp2 from the FMA-pipe polynomial,
+  // the others from MUFU.
   const uint64_t c2 = f2_splat(c);
-  const uint64_t negm2 = f2_splat(neg_m);
-  uint32_t pk[32];
+  uint32_t pk[32];  // pk[2i + e]: row g + 8e, keys 8i + 2q, 8i + 2q + 1 (16x128b fragment)
   uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
   for (int k = 0; k < 32; ++k) {
-    const uint64_t x =
-        f2_fma(f2_pack(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1])), c2, negm2);
+    const uint64_t x = f2_fma(f2_pack(f(sr[2 * k]), f(sr[2 * k + 1])), c2, negm2[k & 1]);
     float x0, x1, e0, e1;
     f2_unpack(x, x0, x1);
     if ((Cfg::kPolyMask >> (k & 7)) & 1u) {
@@ -477,11 +465,11 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
     acc[k & 3] = f2_add(acc[k & 3], f2_pack(e0, e1));
     pk[k] = pack_half2(e0, e1);
   }
-  float acc0, acc1, acc2, acc3;
-  f2_unpack(f2_add(acc[0], acc[1]), acc0, acc1);
-  f2_unpack(f2_add(acc[2], acc[3]), acc2, acc3);
-  l_run = l_run * alpha + ((acc0 + acc1) + (acc2 + acc3));
-  m_run = m_use;
+  float s0, s1, t0, t1;
+  f2_unpack(f2_add(acc[0], acc[2]), s0, s1);
+  f2_unpack(f2_add(acc[1], acc[3]), t0, t1);
+  l_run[0] = l_run[0] * alpha[0] + (s0 + s1);
+  l_run[1] = l_run[1] * alpha[1] + (t0 + t1);
 
   // P and O are free once the previous O += P V has completed.
   if (g > 0) {
@@ -490,13 +478,13 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
       return false;
     tc_fence_after();
   }
-  tmem_st32(tP, pk);
+  tmem_st_16x128b_x16(tP, pk);
   if (grow && !first) {
-    uint32_t o[32];
-    tmem_ld32_sync(tO, o);
+    uint32_t o[32];  // o[4i + e]: row g + 8 (e / 2), d 8i + 2q + e % 2
+    tmem_ld_16x256b_x8_sync(tO, o);
 #pragma unroll
-    for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-    tmem_st32(tO, o);
+    for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(f(o[k]) * alpha[(k >> 1) & 1]);
+    tmem_st_16x256b_x8(tO, o);
   }
   tmem_wait_st();
   tc_fence_before();
@@ -511,26 +499,27 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int quad = warp & 3;              // TMEM lane quadrant this warp may access
-  const int half = (warp >> 2) & 1;       // which 64 of the tile's 128 key columns
-  const int row = quad * 32 + lane;       // row of the query tile == TMEM lane
-  const uint32_t lane_bits = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t tS = tmem + lane_bits + Cfg::kColS + 128 * tile + 64 * half;
-  const uint32_t tS_other = tmem + lane_bits + Cfg::kColS + 128 * tile + 64 * (half ^ 1);
-  const uint32_t tP = tmem + lane_bits + Cfg::kColP + 64 * tile + 32 * half;
-  const uint32_t tO = tmem + lane_bits + Cfg::kColO + 64 * tile + 32 * half;
-  float* xch = reinterpret_cast<float*>(smem + Cfg::kXchOff);  // [tile][half][row] row sums
+  // Warp w of the tile may only reach TMEM lane quadrant w % 4; the two warps of a quadrant
+  // take its upper and lower 16 rows.
+  const int slice = (warp & 3) * 32 + ((warp >> 2) & 1) * 16;  // first tile row of this warp
+  const int gq = lane >> 2;                                     // rows slice + gq, + gq + 8
+  const int q = lane & 3;
+  const uint32_t lane_bits = static_cast<uint32_t>(slice) << 16;
+  const uint32_t tS = tmem + lane_bits + Cfg::kColS + 128 * tile;
+  const uint32_t tP = tmem + lane_bits + Cfg::kColP + 64 * tile;
+  const uint32_t tO = tmem + lane_bits + Cfg::kColO + 64 * tile;
+  const bool tile_leader = (warp & 7) == 0 && lane == 0;
 
   int g = 0;       // global step index (phase of the per-step barriers)
   int stores = 0;  // whole units stored so far (phase of the staging barrier)
   StepCursor cur;
   cur.init(p);
   while (cur.valid()) {
-    float m_run = -INFINITY;  // running max of s*scale*log2(e), identical in both threads
-    float l_run = 0.0f;       // this thread's partial sum of p over its column half
+    float m_run[2] = {-INFINITY, -INFINITY};  // running max of s*scale*log2(e), per row
+    float l_run[2] = {0.0f, 0.0f};            // this thread's partial row sums
     for (int j = cur.j0; j < cur.j1; ++j, ++g) {
-      if (!softmax_step<Cfg>(p, bars, tS, tS_other, tP, tO, tile, half, lane, g, j, j == cur.j0,
-                             m_run, l_run, wd))
+      if (!softmax_step<Cfg>(p, bars, tS, tP, tO, tile, lane, g, j, j == cur.j0, m_run, l_run,
+                             wd))
         return;
     }
     // ---- unit epilogue (g - 1 is the unit's last step)
@@ -538,43 +527,35 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
                    kSiteSoftOFinal))
       return;
     tc_fence_after();
-    // Row sum = both halves' partial sums (the one place the two threads of a row meet).
-    float* my = xch + (tile * 2 + half) * Cfg::kRows + row;
-    float* other = xch + (tile * 2 + (half ^ 1)) * Cfg::kRows + row;
-    *my = l_run;
-    {
-      const int xb = Cfg::kBarXchSum + tile * 4 + quad;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(xb));
-      if (!wait_warp(bar(xb), static_cast<uint32_t>(cur.seg_idx) & 1u, wd, kSiteSoftXch)) return;
+    float l_row[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      l_row[r] = l_run[r] + __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+      l_row[r] += __shfl_xor_sync(0xffffffffu, l_row[r], 2);
     }
-    const float l_row = l_run + *other;
-    uint32_t o[32];
-    tmem_ld32_sync(tO, o);
+    uint32_t o[32];  // o[4i + e]: row gq + 8 (e / 2), d 8i + 2q + e % 2
+    tmem_ld_16x256b_x8_sync(tO, o);
     tc_fence_before();
     const int b = cur.seg_idx & 1;
     if (cur.whole(p.nkb)) {
       // O / l -> fp16 -> swizzled staging (this tile's slot of the unit's Q buffer) -> TMA.
       uint8_t* stage = smem + Cfg::kQOff + (b * Cfg::NQ + tile) * Cfg::kTileBytes;
-      const float inv_l = 1.0f / l_row;
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {  // 4 chunks of 8 halves = 16 bytes each
-        uint32_t w[4];
+      for (int r = 0; r < 2; ++r) {
+        const int row = slice + gq + 8 * r;
+        const float inv_l = 1.0f / l_row[r];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          w[e] = pack_half2(__uint_as_float(o[8 * ch + 2 * e]) * inv_l,
-                            __uint_as_float(o[8 * ch + 2 * e + 1]) * inv_l);
+        for (int i = 0; i < 8; ++i) {  // 16-byte chunk i of the row, 4 bytes per thread
+          const uint32_t w = pack_half2(__uint_as_float(o[4 * i + 2 * r]) * inv_l,
+                                        __uint_as_float(o[4 * i + 2 * r + 1]) * inv_l);
+          const uint32_t dst = smem_addr(stage + row * 128 + ((i ^ (row & 7)) << 4) + 4 * q);
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst), "r"(w) : "memory");
         }
-        const int chunk = 4 * half + ch;
-        const uint32_t dst = smem_addr(stage + row * 128 + ((chunk ^ (row & 7)) << 4));
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w[0]),
-                     "r"(w[1]), "r"(w[2]), "r"(w[3])
-                     : "memory");
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(Cfg::kBarStage + tile));
-      if (half == 0 && row == 0) {
+      if (tile_leader) {
         // the tile's eight warps have written their staging rows: store, then free the
         // Q buffer once the store has read it
         if (!wait_single(bar(Cfg::kBarStage + tile), static_cast<uint32_t>(stores) & 1u, wd,
@@ -595,20 +576,21 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
       float* ws = p.workspace +
                   static_cast<size_t>(2 * blockIdx.x + (cur.first_of_range() ? 0 : 1)) *
                       Cfg::kSlotFloats;
-      const int r = tile * Cfg::kRows + row;
-      float4* dst =
-          reinterpret_cast<float4*>(ws + static_cast<size_t>(r) * Cfg::kHeadDim + 32 * half);
 #pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4) {
-        dst[q4] = make_float4(__uint_as_float(o[4 * q4]), __uint_as_float(o[4 * q4 + 1]),
-                              __uint_as_float(o[4 * q4 + 2]), __uint_as_float(o[4 * q4 + 3]));
-      }
-      if (half == 0) {
-        ws[Cfg::kRowsPerUnit * Cfg::kHeadDim + r] = m_run;
-        ws[Cfg::kRowsPerUnit * (Cfg::kHeadDim + 1) + r] = l_row;
+      for (int r = 0; r < 2; ++r) {
+        const int row = tile * Cfg::kRows + slice + gq + 8 * r;
+        float2* dst = reinterpret_cast<float2*>(ws + static_cast<size_t>(row) * Cfg::kHeadDim);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[4 * i + q] = make_float2(__uint_as_float(o[4 * i + 2 * r]),
+                                       __uint_as_float(o[4 * i + 2 * r + 1]));
+        if (q == 0) {
+          ws[Cfg::kRowsPerUnit * Cfg::kHeadDim + row] = m_run[r];
+          ws[Cfg::kRowsPerUnit * (Cfg::kHeadDim + 1) + row] = l_row[r];
+        }
       }
       // the Q buffer was only read by this unit's S MMAs, all complete by now
-      if (half == 0 && row == 0) mbar_arrive(bar(Cfg::kBarQEmpty + b));
+      if (tile_leader) mbar_arrive(bar(Cfg::kBarQEmpty + b));
     }
     cur.next_segment(p);
   }
@@ -646,7 +628,6 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
       mbar_init(bars + 8 * (Cfg::kBarPFull + i), 8);
       mbar_init(bars + 8 * (Cfg::kBarODone + i), 1);
     }
-    for (int x = 0; x < NQ * 4; ++x) mbar_init(bars + 8 * (Cfg::kBarXchSum + x), 2);
     for (int i = 0; i < NQ; ++i) mbar_init(bars + 8 * (Cfg::kBarStage + i), 8);
     mbar_init(bars + 8 * Cfg::kBarDrain, 1);
     mbar_init_fence();
