@@ -140,6 +140,24 @@ int encode_bhnd(CUtensorMap* map, const void* base, int64_t n, int64_t bh) {
   return MFA_OK;
 }
 
+// Launches the split-mode merge as a programmatic dependent of the forward kernel just
+// queued on `stream` (it may start while the forward kernel drains; it reads the workspace
+// only after griddepcontrol.wait).
+template <class Cfg>
+cudaError_t launch_merge(const MergeParams& mp, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(mp.ctas));
+  cfg.blockDim = dim3(Cfg::kRowsPerUnit * kMergeThreadsPerRow);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats>, mp);
+}
+
 // Persistent launch: one CTA per SM (or fewer for small problems). When whole query blocks
 // divide badly over the SMs (more than 3% idle in the last wave), the key dimension is split
 // too and a merge kernel combines the pieces; the partial results live in a stream-ordered
@@ -207,9 +225,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
     mp.q_blocks = p.q_blocks;
     mp.nkb = p.nkb;
     mp.ctas = static_cast<int>(ctas);
-    mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats>
-        <<<static_cast<unsigned>(ctas), Cfg::kRowsPerUnit, 0, stream>>>(mp);
-    e = cudaGetLastError();
+    e = launch_merge<Cfg>(mp, stream);
   }
   if (split) {
     const cudaError_t ef = cudaFreeAsync(p.workspace, stream);
@@ -357,9 +373,7 @@ int launch_forward_noalloc(const void* q, const void* k, const void* v, void* ou
     mp.q_blocks = p.q_blocks;
     mp.nkb = p.nkb;
     mp.ctas = static_cast<int>(ctas);
-    mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats>
-        <<<static_cast<unsigned>(ctas), Cfg::kRowsPerUnit, 0, stream>>>(mp);
-    e = cudaGetLastError();
+    e = launch_merge<Cfg>(mp, stream);
   }
   if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
   return MFA_OK;

@@ -610,6 +610,9 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kTmemSlotOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kAbortOff);
 
+  // The split-mode merge kernel may be scheduled now; it waits for this grid to complete
+  // before reading anything this grid writes.
+  if (threadIdx.x == 0) grid_dependents_launch();
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int b = 0; b < 2; ++b) {
@@ -670,19 +673,29 @@ struct MergeParams {
 
 // One CTA per forward CTA c; it merges the query block that starts inside c's range and
 // continues past it (if any): every piece's O is rescaled to the common row max, summed,
-// divided by the rescaled sum of row sums, rounded to fp16. One thread per query row.
+// divided by the rescaled sum of row sums, rounded to fp16. Four threads per query row, each
+// on every fourth 16-byte chunk of it, so a warp reads 8 rows x 256 contiguous bytes.
+// Launched as a programmatic dependent of the forward kernel: the index work overlaps the
+// forward kernel's tail, and griddepcontrol.wait holds the workspace reads until the forward
+// grid has completed and its writes are visible.
+constexpr int kMergeThreadsPerRow = 4;
+
 template <int kRowsPerUnit, int kSlotFloats>
-__global__ void __launch_bounds__(kRowsPerUnit) mfa_merge_kernel(const MergeParams mp) {
+__global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
+    mfa_merge_kernel(const MergeParams mp) {
   constexpr int kD = 64;
+  constexpr int kChunks = kD / 4 / kMergeThreadsPerRow;  // float4 chunks per thread
   const int c = static_cast<int>(blockIdx.x);
   const long long units = static_cast<long long>(mp.bh) * mp.q_blocks;
   long long b0, b1;
   cta_range(units, mp.nkb, 1, c, mp.ctas, b0, b1);
-  if (b1 <= b0) return;
-  const long long u = (b1 - 1) / mp.nkb;  // query block holding c's last key block
-  if ((u + 1) * mp.nkb <= b1) return;     // it ends inside c: not split here
-  if (u * mp.nkb < b0) return;            // it started in an earlier CTA: merged there
-  const int r = static_cast<int>(threadIdx.x);
+  const long long u = b1 > b0 ? (b1 - 1) / mp.nkb : 0;  // query block holding c's last step
+  // Merged here only if it starts inside c and ends past it.
+  const bool mine = b1 > b0 && (u + 1) * mp.nkb > b1 && u * mp.nkb >= b0;
+  grid_dependency_wait();
+  if (!mine) return;
+  const int r = static_cast<int>(threadIdx.x) / kMergeThreadsPerRow;
+  const int k = static_cast<int>(threadIdx.x) % kMergeThreadsPerRow;
   // Pieces: c's last segment (its first too if c's range starts exactly at u), then the
   // first segment of every following CTA that overlaps u.
   auto piece = [&](int cc) {
@@ -696,9 +709,9 @@ __global__ void __launch_bounds__(kRowsPerUnit) mfa_merge_kernel(const MergePara
   };
   float m_max = -INFINITY;
   for (int cc = c; overlaps(cc); ++cc) m_max = fmaxf(m_max, piece(cc)[kRowsPerUnit * kD + r]);
-  float acc[kD];
+  float4 acc[kChunks];
 #pragma unroll
-  for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
+  for (int i = 0; i < kChunks; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   float l = 0.0f;
   for (int cc = c; overlaps(cc); ++cc) {
     const float* ws = piece(cc);
@@ -706,28 +719,26 @@ __global__ void __launch_bounds__(kRowsPerUnit) mfa_merge_kernel(const MergePara
     l += w * ws[kRowsPerUnit * (kD + 1) + r];
     const float4* o = reinterpret_cast<const float4*>(ws + static_cast<size_t>(r) * kD);
 #pragma unroll
-    for (int q4 = 0; q4 < kD / 4; ++q4) {
-      const float4 v = o[q4];
-      acc[4 * q4] += w * v.x;
-      acc[4 * q4 + 1] += w * v.y;
-      acc[4 * q4 + 2] += w * v.z;
-      acc[4 * q4 + 3] += w * v.w;
+    for (int i = 0; i < kChunks; ++i) {
+      const float4 v = o[kMergeThreadsPerRow * i + k];
+      acc[i].x += w * v.x;
+      acc[i].y += w * v.y;
+      acc[i].z += w * v.z;
+      acc[i].w += w * v.w;
     }
   }
   const int head = static_cast<int>(u / mp.q_blocks);
   const int qrow = static_cast<int>(u % mp.q_blocks) * kRowsPerUnit + r;
   if (qrow >= mp.n) return;
   const float inv_l = 1.0f / l;
-  uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(mp.out) +
+  uint2* dst = reinterpret_cast<uint2*>(static_cast<__half*>(mp.out) +
                                         (static_cast<size_t>(head) * mp.n + qrow) * kD);
 #pragma unroll
-  for (int q8 = 0; q8 < kD / 8; ++q8) {
-    uint4 w;
-    w.x = pack_half2(acc[8 * q8] * inv_l, acc[8 * q8 + 1] * inv_l);
-    w.y = pack_half2(acc[8 * q8 + 2] * inv_l, acc[8 * q8 + 3] * inv_l);
-    w.z = pack_half2(acc[8 * q8 + 4] * inv_l, acc[8 * q8 + 5] * inv_l);
-    w.w = pack_half2(acc[8 * q8 + 6] * inv_l, acc[8 * q8 + 7] * inv_l);
-    dst[q8] = w;
+  for (int i = 0; i < kChunks; ++i) {
+    uint2 w;
+    w.x = pack_half2(acc[i].x * inv_l, acc[i].y * inv_l);
+    w.y = pack_half2(acc[i].z * inv_l, acc[i].w * inv_l);
+    dst[kMergeThreadsPerRow * i + k] = w;
   }
 }
 

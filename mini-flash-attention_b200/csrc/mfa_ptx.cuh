@@ -64,6 +64,16 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// Programmatic dependent launch: let the next kernel of the stream be scheduled (issued by
+// the primary grid) / wait until the primary grid has completed and its memory operations
+// are visible (issued by the dependent grid; returns at once without a primary).
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void sleep_ns(uint32_t ns) {
   asm volatile("nanosleep.u32 %0;" ::"r"(ns));
 }
