@@ -31,7 +31,7 @@ enum mfa_status_code {
   MFA_ERR_INVALID_ARGUMENT = 1, /* null / misaligned pointer, negative or oversized extent */
   MFA_ERR_HEAD_DIM = 2,         /* D != 64 */
   MFA_ERR_SEQ_LEN = 3,          /* N not a multiple of the entry point's block size */
-  MFA_ERR_CAUSAL = 4,           /* causal masking requested from an entry point without it */
+  MFA_ERR_CAUSAL = 4,           /* reserved: causal masking is supported by every entry point */
   MFA_ERR_CUDA = 5,             /* CUDA runtime or driver error; message has the details */
   MFA_ERR_DEVICE = 6            /* current device is not an sm_100 (B200-class) GPU */
 };
@@ -39,9 +39,11 @@ enum mfa_status_code {
 /*
  * Attention forward, tcgen05 kernel with two query tiles (256 rows) per CTA.
  * Replaces the reference launcher launch_flash_attn_forward
- * (src/mini_flash_attention/flash_attn_cuda.cu:370-420): same arguments, same checks in the
- * same order (D == 64, N % 128 == 0, causal == 0) with the same messages. `scale` multiplies
- * q.k before the softmax (the reference binding passes 1/sqrt(D), flash_attn.cpp:94).
+ * (src/mini_flash_attention/flash_attn_cuda.cu:370-420): same arguments, the same D == 64 and
+ * N % 128 == 0 checks in the same order with the same messages. `scale` multiplies q.k before
+ * the softmax (the reference binding passes 1/sqrt(D), flash_attn.cpp:94). causal != 0 masks
+ * key index > query index (the reference launcher rejects causal, flash_attn_cuda.cu:408-410;
+ * the mask is the one its test and benchmark build, tests/test_forward.py:30-32).
  * bh == 0 or n == 0 is a no-op that returns MFA_OK.
  */
 MFA_API int mfa_fwd_f16(const void* q, const void* k, const void* v, void* out, int64_t bh, int64_t n,
@@ -51,8 +53,9 @@ MFA_API int mfa_fwd_f16(const void* q, const void* k, const void* v, void* out, 
  * Attention forward, single-query-tile tcgen05 kernel (128 rows per CTA, 2-stage K/V ring).
  * Replaces the reference's WMMA launcher, declared as launch_flash_attn_forward_wmma
  * (src/mini_flash_attention/flash_attn.cpp:21-31) and implemented at
- * src/mini_flash_attention/flash_attn_wmma_cuda.cu:253-289: checks D == 64, N % 64 == 0,
- * causal == 0 with that launcher's messages.
+ * src/mini_flash_attention/flash_attn_wmma_cuda.cu:253-289: checks D == 64 and N % 64 == 0
+ * with that launcher's messages; causal != 0 masks key index > query index (that launcher
+ * rejects causal, flash_attn_wmma_cuda.cu:275-277).
  */
 MFA_API int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, void* out, int64_t bh,
                        int64_t n, int32_t d, float scale, int32_t causal, void* stream);

@@ -31,8 +31,16 @@ __device__ int g_device_status = 0;
 
 unsigned long long g_watchdog_ns = 2000000000ull;  // 2 s per wait
 
-using FullKernel = FwdConfig<2, 3>;
-using SimpleKernel = FwdConfig<1, 2>;
+using FullKernel = FwdConfig<2, 3, false>;
+using FullCausal = FwdConfig<2, 3, true>;
+using SimpleKernel = FwdConfig<1, 2, false>;
+using SimpleCausal = FwdConfig<1, 2, true>;
+
+template <class Cfg>
+cudaError_t set_smem_attribute() {
+  return cudaFuncSetAttribute(mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+}
 
 struct DeviceState {
   std::once_flag once;
@@ -92,13 +100,10 @@ int prepare_device(int dev) {
       return;
     }
     e = cudaDeviceGetAttribute(&ds.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(mfa_fwd_kernel<FullKernel::NQ, FullKernel::STAGES>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, FullKernel::kSmemBytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(mfa_fwd_kernel<SimpleKernel::NQ, SimpleKernel::STAGES>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SimpleKernel::kSmemBytes);
+    if (e == cudaSuccess) e = set_smem_attribute<FullKernel>();
+    if (e == cudaSuccess) e = set_smem_attribute<FullCausal>();
+    if (e == cudaSuccess) e = set_smem_attribute<SimpleKernel>();
+    if (e == cudaSuccess) e = set_smem_attribute<SimpleCausal>();
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status_ptr), g_device_status);
     if (e == cudaSuccess) {
       // A private stream-ordered pool for the split-mode partial results: the scratch is
@@ -155,13 +160,87 @@ cudaError_t launch_merge(const MergeParams& mp, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats>, mp);
+  return cudaLaunchKernelEx(
+      &cfg, mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats, Cfg::kCausal>, mp);
 }
 
-// Persistent launch: one CTA per SM (or fewer for small problems). When whole query blocks
-// divide badly over the SMs (more than 3% idle in the last wave), the key dimension is split
-// too and a merge kernel combines the pieces; the partial results live in a stream-ordered
-// scratch allocation freed on the same stream.
+// Launch plan, shared by every entry point. Persistent: one CTA per SM (or fewer for small
+// problems). When whole query blocks divide badly over the SMs (more than 3% idle in the last
+// wave), and always with causal masking (query blocks of unequal length), the global steps
+// are split evenly over the CTAs and a merge kernel combines the pieces of the query blocks
+// cut by a CTA boundary.
+struct Plan {
+  Schedule sc;
+  int64_t ctas = 0;
+  int split = 0;
+  size_t workspace_bytes = 0;  // split mode: partial-result slots
+};
+
+template <class Cfg>
+int plan_forward(int64_t bh, int64_t n, int64_t sms, Plan& pl) {
+  const int64_t q_blocks = (n + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
+  const int64_t nkb = (n + Cfg::kKeys - 1) / Cfg::kKeys;
+  const int64_t units = q_blocks * bh;
+  if (static_cast<double>(units) * static_cast<double>(nkb) > static_cast<double>(int64_t(1) << 40) ||
+      units > 0x7fffffffLL)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  pl.sc = make_schedule(bh, n, Cfg::kRowsPerUnit, Cfg::kKeys, Cfg::kCausal);
+  const int64_t total = pl.sc.total();
+  pl.ctas = units < sms ? units : sms;
+  pl.split = 0;
+  if (Cfg::kCausal) {
+    pl.split = 1;
+  } else if (units % sms != 0 && units < 32 * sms) {
+    // idle fraction of the last wave if only whole query blocks are handed out
+    const double waves = static_cast<double>(units) / sms;
+    const double busy = waves / static_cast<double>((units + sms - 1) / sms);
+    if (busy < 0.97) pl.split = 1;
+  }
+  if (pl.split) pl.ctas = total < sms ? total : sms;
+  // every CTA's work must stay below 2^31 steps (32-bit step counters in the kernel)
+  if ((pl.split ? total / pl.ctas + 1 : (units + pl.ctas - 1) / pl.ctas * nkb) >= 0x7fffffffLL)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  pl.workspace_bytes =
+      pl.split ? static_cast<size_t>(2 * pl.ctas) * Cfg::kSlotFloats * sizeof(float) : 0;
+  return MFA_OK;
+}
+
+// Queues the forward kernel (and the merge kernel in split mode) of plan `pl` on `stream`;
+// `workspace` holds pl.workspace_bytes.
+template <class Cfg>
+cudaError_t launch_planned(const void* q, const void* k, const void* v, void* out, int64_t bh,
+                           int64_t n, float scale, const Plan& pl, float* workspace,
+                           int* status_ptr, cudaStream_t stream, int* rc) {
+  FwdParams p;
+  *rc = MFA_OK;
+  if ((*rc = encode_bhnd(&p.tm_q, q, n, bh)) != MFA_OK) return cudaSuccess;
+  if ((*rc = encode_bhnd(&p.tm_k, k, n, bh)) != MFA_OK) return cudaSuccess;
+  if ((*rc = encode_bhnd(&p.tm_v, v, n, bh)) != MFA_OK) return cudaSuccess;
+  if ((*rc = encode_bhnd(&p.tm_o, out, n, bh)) != MFA_OK) return cudaSuccess;
+  p.n = static_cast<int>(n);
+  p.sc = pl.sc;
+  p.split = pl.split;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.timeout_ns = g_watchdog_ns;
+  p.status = status_ptr;
+  p.workspace = workspace;
+  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal>
+      <<<static_cast<unsigned>(pl.ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && pl.split) {
+    MergeParams mp;
+    mp.out = out;
+    mp.workspace = workspace;
+    mp.n = p.n;
+    mp.sc = pl.sc;
+    mp.ctas = static_cast<int>(pl.ctas);
+    e = launch_merge<Cfg>(mp, stream);
+  }
+  return e;
+}
+
+// The split plan's partial results live in a stream-ordered scratch allocation from a private
+// pool, freed on the same stream.
 template <class Cfg>
 int launch_forward(const void* q, const void* k, const void* v, void* out, int64_t bh, int64_t n,
                    float scale, cudaStream_t stream) {
@@ -171,66 +250,21 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
   int rc = prepare_device(dev);
   if (rc != MFA_OK) return rc;
-
-  FwdParams p;
-  if ((rc = encode_bhnd(&p.tm_q, q, n, bh)) != MFA_OK) return rc;
-  if ((rc = encode_bhnd(&p.tm_k, k, n, bh)) != MFA_OK) return rc;
-  if ((rc = encode_bhnd(&p.tm_v, v, n, bh)) != MFA_OK) return rc;
-  if ((rc = encode_bhnd(&p.tm_o, out, n, bh)) != MFA_OK) return rc;
-  const int64_t q_blocks = (n + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
-  const int64_t nkb = (n + Cfg::kKeys - 1) / Cfg::kKeys;
-  const int64_t units = q_blocks * bh;
-  if (units > (int64_t(1) << 40) / nkb)
-    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  const int64_t sms = g_devices[dev].num_sms;
-  if (units > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  int64_t ctas = units < sms ? units : sms;
-  int split = 0;
-  if (units % sms != 0 && units < 32 * sms) {
-    // idle fraction of the last wave if only whole query blocks are handed out
-    const double waves = static_cast<double>(units) / sms;
-    const double busy = waves / static_cast<double>((units + sms - 1) / sms);
-    if (busy < 0.97) {
-      split = 1;
-      ctas = units * nkb < sms ? units * nkb : sms;
-    }
-  }
-  // every CTA's work must stay below 2^31 steps (32-bit step counters in the kernel)
-  if ((split ? units * nkb / ctas : (units + ctas - 1) / ctas * nkb) >= 0x7fffffffLL)
-    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  p.n = static_cast<int>(n);
-  p.bh = static_cast<int>(bh);
-  p.q_blocks = static_cast<int>(q_blocks);
-  p.nkb = static_cast<int>(nkb);
-  p.split = split;
-  p.scale_log2 = scale * 1.4426950408889634f;
-  p.timeout_ns = g_watchdog_ns;
-  p.status = g_devices[dev].status_ptr;
-  p.workspace = nullptr;
-  if (split) {
-    const size_t bytes = static_cast<size_t>(2 * ctas) * Cfg::kSlotFloats * sizeof(float);
-    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&p.workspace), bytes,
+  Plan pl;
+  if ((rc = plan_forward<Cfg>(bh, n, g_devices[dev].num_sms, pl)) != MFA_OK) return rc;
+  float* workspace = nullptr;
+  if (pl.split) {
+    e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&workspace), pl.workspace_bytes,
                                 g_devices[dev].pool, stream);
     if (e != cudaSuccess) return fail_cuda(e, "cudaMallocFromPoolAsync (split workspace)");
   }
-  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES>
-      <<<static_cast<unsigned>(ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  e = cudaGetLastError();
-  if (e == cudaSuccess && split) {
-    MergeParams mp;
-    mp.out = out;
-    mp.workspace = p.workspace;
-    mp.n = p.n;
-    mp.bh = p.bh;
-    mp.q_blocks = p.q_blocks;
-    mp.nkb = p.nkb;
-    mp.ctas = static_cast<int>(ctas);
-    e = launch_merge<Cfg>(mp, stream);
-  }
-  if (split) {
-    const cudaError_t ef = cudaFreeAsync(p.workspace, stream);
+  e = launch_planned<Cfg>(q, k, v, out, bh, n, scale, pl, workspace,
+                          g_devices[dev].status_ptr, stream, &rc);
+  if (pl.split) {
+    const cudaError_t ef = cudaFreeAsync(workspace, stream);
     if (e == cudaSuccess) e = ef;
   }
+  if (rc != MFA_OK) return rc;
   if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
   return MFA_OK;
 }
@@ -288,9 +322,8 @@ int prepare_noalloc(int dev) {
       return;
     }
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(mfa_fwd_kernel<FullKernel::NQ, FullKernel::STAGES>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, FullKernel::kSmemBytes);
+    if (e == cudaSuccess) e = set_smem_attribute<FullKernel>();
+    if (e == cudaSuccess) e = set_smem_attribute<FullCausal>();
     if (e == cudaSuccess)
       e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status_ptr), g_device_status);
     if (e == cudaSuccess)
@@ -304,11 +337,11 @@ int prepare_noalloc(int dev) {
   return MFA_OK;
 }
 
-// launch_forward's plan (CTA count, split decision) with the split workspace taken from the
-// static scratch instead of a stream-ordered allocation.
+// launch_forward with the split workspace taken from the static scratch instead of a
+// stream-ordered allocation.
+template <class Cfg>
 int launch_forward_noalloc(const void* q, const void* k, const void* v, void* out, int64_t bh,
                            int64_t n, float scale, cudaStream_t stream) {
-  using Cfg = FullKernel;
   if (bh == 0 || n == 0) return MFA_OK;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -316,65 +349,18 @@ int launch_forward_noalloc(const void* q, const void* k, const void* v, void* ou
   int rc = prepare_noalloc(dev);
   if (rc != MFA_OK) return rc;
   const NoAllocState& st = g_noalloc[dev];
-
-  FwdParams p;
-  if ((rc = encode_bhnd(&p.tm_q, q, n, bh)) != MFA_OK) return rc;
-  if ((rc = encode_bhnd(&p.tm_k, k, n, bh)) != MFA_OK) return rc;
-  if ((rc = encode_bhnd(&p.tm_v, v, n, bh)) != MFA_OK) return rc;
-  if ((rc = encode_bhnd(&p.tm_o, out, n, bh)) != MFA_OK) return rc;
-  const int64_t q_blocks = (n + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
-  const int64_t nkb = (n + Cfg::kKeys - 1) / Cfg::kKeys;
-  const int64_t units = q_blocks * bh;
-  if (units > (int64_t(1) << 40) / nkb)
-    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  const int64_t sms = st.num_sms;
-  if (units > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  int64_t ctas = units < sms ? units : sms;
-  int split = 0;
-  if (units % sms != 0 && units < 32 * sms) {
-    const double waves = static_cast<double>(units) / sms;
-    const double busy = waves / static_cast<double>((units + sms - 1) / sms);
-    if (busy < 0.97) {
-      split = 1;
-      ctas = units * nkb < sms ? units * nkb : sms;
-    }
-  }
-  if ((split ? units * nkb / ctas : (units + ctas - 1) / ctas * nkb) >= 0x7fffffffLL)
-    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  p.n = static_cast<int>(n);
-  p.bh = static_cast<int>(bh);
-  p.q_blocks = static_cast<int>(q_blocks);
-  p.nkb = static_cast<int>(nkb);
-  p.split = split;
-  p.scale_log2 = scale * 1.4426950408889634f;
-  p.timeout_ns = g_watchdog_ns;
-  p.status = st.status_ptr;
-  p.workspace = nullptr;
-  if (split) {
-    // Every slot the merge kernel reads is written by the forward kernel of the same call, so
-    // nothing in the scratch has to start at zero.
-    const size_t bytes = static_cast<size_t>(2 * ctas) * Cfg::kSlotFloats * sizeof(float);
-    if (bytes > MFA_NOALLOC_SCRATCH_BYTES)
-      return fail(MFA_ERR_INVALID_ARGUMENT,
-                  "mfa_fwd_f16_noalloc: this launch needs " + std::to_string(bytes) +
-                      " bytes of scratch, more than its static " +
-                      std::to_string(MFA_NOALLOC_SCRATCH_BYTES) + "-byte array");
-    p.workspace = st.scratch;
-  }
-  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES>
-      <<<static_cast<unsigned>(ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  e = cudaGetLastError();
-  if (e == cudaSuccess && split) {
-    MergeParams mp;
-    mp.out = out;
-    mp.workspace = p.workspace;
-    mp.n = p.n;
-    mp.bh = p.bh;
-    mp.q_blocks = p.q_blocks;
-    mp.nkb = p.nkb;
-    mp.ctas = static_cast<int>(ctas);
-    e = launch_merge<Cfg>(mp, stream);
-  }
+  Plan pl;
+  if ((rc = plan_forward<Cfg>(bh, n, st.num_sms, pl)) != MFA_OK) return rc;
+  // Every slot the merge kernel reads is written by the forward kernel of the same call, so
+  // nothing in the scratch has to start at zero.
+  if (pl.workspace_bytes > MFA_NOALLOC_SCRATCH_BYTES)
+    return fail(MFA_ERR_INVALID_ARGUMENT,
+                "mfa_fwd_f16_noalloc: this launch needs " + std::to_string(pl.workspace_bytes) +
+                    " bytes of scratch, more than its static " +
+                    std::to_string(MFA_NOALLOC_SCRATCH_BYTES) + "-byte array");
+  e = launch_planned<Cfg>(q, k, v, out, bh, n, scale, pl, pl.split ? st.scratch : nullptr,
+                          st.status_ptr, stream, &rc);
+  if (rc != MFA_OK) return rc;
   if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
   return MFA_OK;
 }
@@ -416,12 +402,14 @@ extern "C" int mfa_fwd_f16(const void* q, const void* k, const void* v, void* ou
                            int64_t n, int32_t d, float scale, int32_t causal, void* stream) {
   int rc = check_common(q, k, v, out, bh, n, d);
   if (rc != MFA_OK) return rc;
-  // Same checks and messages, in the same order, as flash_attn_cuda.cu:399-410.
+  // The D and N checks and messages of flash_attn_cuda.cu:399-407, in that order. Causal
+  // masking (rejected by flash_attn_cuda.cu:408-410) is supported.
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
   if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
-  if (causal) return fail(MFA_ERR_CAUSAL, "Causal attention is not supported yet");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
-  return launch_forward<FullKernel>(q, k, v, out, bh, n, scale, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return causal ? launch_forward<FullCausal>(q, k, v, out, bh, n, scale, s)
+                : launch_forward<FullKernel>(q, k, v, out, bh, n, scale, s);
 }
 
 extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, void* out,
@@ -429,14 +417,15 @@ extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, v
                                   void* stream) {
   int rc = check_common(q, k, v, out, bh, n, d);
   if (rc != MFA_OK) return rc;
-  // Same checks and messages, in the same order, as flash_attn_wmma_cuda.cu:269-277.
+  // The D and N checks and messages of flash_attn_wmma_cuda.cu:269-274, in that order.
+  // Causal masking (rejected by flash_attn_wmma_cuda.cu:275-277) is supported.
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This WMMA prototype supports only D=64 yet");
   if (n % 64 != 0)
     return fail(MFA_ERR_SEQ_LEN, "Only N (seq len) divisible by 64 and 64 are supported yet");
-  if (causal) return fail(MFA_ERR_CAUSAL, "Causal attention is not yet supported");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
-  return launch_forward<SimpleKernel>(q, k, v, out, bh, n, scale,
-                                      static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return causal ? launch_forward<SimpleCausal>(q, k, v, out, bh, n, scale, s)
+                : launch_forward<SimpleKernel>(q, k, v, out, bh, n, scale, s);
 }
 
 extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, void* out,
@@ -446,9 +435,10 @@ extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, 
   if (rc != MFA_OK) return rc;
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
   if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
-  if (causal) return fail(MFA_ERR_CAUSAL, "Causal attention is not supported yet");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
-  return launch_forward_noalloc(q, k, v, out, bh, n, scale, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return causal ? launch_forward_noalloc<FullCausal>(q, k, v, out, bh, n, scale, s)
+                : launch_forward_noalloc<FullKernel>(q, k, v, out, bh, n, scale, s);
 }
 
 extern "C" const char* mfa_last_error_string(void) { return g_last_error.c_str(); }

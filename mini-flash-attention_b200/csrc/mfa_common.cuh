@@ -6,6 +6,7 @@
 #include <cstdint>
 
 #include "mfa_ptx.cuh"
+#include "mfa_schedule.cuh"
 
 namespace mfa {
 
@@ -15,14 +16,12 @@ struct FwdParams {
   CUtensorMap tm_v;
   CUtensorMap tm_o;
   int n;                      // sequence length (keys == queries)
-  int bh;                     // batch * heads
-  int q_blocks;               // query blocks per head: ceil(n / rows per CTA pass)
-  int nkb;                    // key blocks per row: ceil(n / keys per block)
-  // Persistent schedule: the units (head, query block, key block), in that row-major order,
-  // are cut into gridDim.x contiguous ranges, one per CTA. split == 0 puts the cuts on whole
-  // query blocks; split == 1 cuts anywhere and a query block processed in pieces by several
-  // CTAs leaves partial results (unnormalised O, row max, row sum) in `workspace`, which the
-  // merge kernel combines.
+  Schedule sc;                // query blocks, key blocks and steps (mfa_schedule.cuh)
+  // Persistent schedule. split == 0 (never with causal masking): whole query blocks, CTA c
+  // takes units c, c + gridDim.x, ... . split == 1: the global steps are cut into gridDim.x
+  // contiguous ranges of equal length; a query block processed in pieces by several CTAs
+  // leaves partial results (unnormalised O, row max, row sum) in `workspace`, which the merge
+  // kernel combines.
   int split;
   float scale_log2;           // softmax scale * log2(e)
   unsigned long long timeout_ns;  // per-wait watchdog limit

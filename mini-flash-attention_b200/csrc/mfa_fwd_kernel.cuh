@@ -39,13 +39,15 @@
 #include "mfa_common.cuh"
 #include "mfa_exp2.cuh"
 #include "mfa_ptx.cuh"
+#include "mfa_schedule.cuh"
 
 namespace mfa {
 
-template <int NQ_, int STAGES_>
+template <int NQ_, int STAGES_, bool CAUSAL_>
 struct FwdConfig {
   static constexpr int NQ = NQ_;
   static constexpr int STAGES = STAGES_;
+  static constexpr bool kCausal = CAUSAL_;  // mask key index > query index
   static constexpr int kRows = 128;       // query rows per tile (= MMA M)
   static constexpr int kRowsPerUnit = kRows * NQ;
   static constexpr int kKeys = 128;       // keys per block (= S tile N)
@@ -112,29 +114,18 @@ struct FwdConfig {
 };
 
 // ---------------------------------------------------------------- unit schedule
-// Range of CTA `cta` of `ctas` over the row-major units (head, query block, key block).
-__host__ __device__ inline void cta_range(long long units, int nkb, int split, int cta, int ctas,
-                                          long long& begin, long long& end) {
-  if (split) {
-    const long long total = units * nkb;
-    begin = total * cta / ctas;
-    end = total * (cta + 1) / ctas;
-  } else {
-    begin = units * cta / ctas * nkb;
-    end = units * (cta + 1) / ctas * nkb;
-  }
-}
-
 // Walks the steps (one key block of one query block each) of this CTA's work in order. Two
 // orders, chosen by FwdParams::split:
 //   split == 0: whole query blocks u = cta, cta + ctas, cta + 2 ctas, ... so that the CTAs
 //               running at the same time work on neighbouring query blocks, mostly of the
 //               same head, and its K/V blocks are read from L2 by all of them;
-//   split == 1: the contiguous range cta_range() (a head's K/V then fits in L2 anyway: split
-//               mode is only chosen when there are few query blocks).
+//   split == 1: the contiguous step range split_range() (a head's K/V then fits in L2 anyway:
+//               split mode is chosen when there are few query blocks, or with causal masking,
+//               whose query blocks differ in length).
 // Six 32-bit words of state: it is live across the softmax loop, where registers are scarce
 // (the launcher guarantees fewer than 2^31 units and steps per CTA). In split mode only the
 // range's first segment can start inside a query block and only its last can stop inside one.
+template <bool kCausal>
 struct StepCursor {
   int u;        // current query block, row-major over (head, query block)
   int j;        // current key block
@@ -143,33 +134,35 @@ struct StepCursor {
   int seg_idx;  // index of the current segment
 
   __device__ void init(const FwdParams& p) {
-    const long long units = static_cast<long long>(p.bh) * p.q_blocks;
+    const Schedule& sc = p.sc;
+    const long long units = static_cast<long long>(sc.bh) * sc.q_blocks;
     seg_idx = 0;
     if (!p.split) {
       u = static_cast<int>(blockIdx.x);
       j = j0 = 0;
-      j1 = u < units ? p.nkb : 0;
+      j1 = u < units ? sc.nkb : 0;
       rem = u < units ? static_cast<int>((units - 1 - u) / gridDim.x) : 0;
       return;
     }
     long long b, e;
-    cta_range(units, p.nkb, 1, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), b, e);
+    split_range(sc.total(), static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), b, e);
     if (b >= e) {
       u = j = j0 = j1 = rem = 0;
       return;
     }
-    const long long uu = b / p.nkb;
-    u = static_cast<int>(uu);
-    j0 = j = static_cast<int>(b - uu * p.nkb);
+    sc.locate<kCausal>(b, u, j0);
+    j = j0;
     const long long len = e - b;
-    j1 = len < static_cast<long long>(p.nkb - j0) ? j0 + static_cast<int>(len) : p.nkb;
+    const int avail = sc.steps_of<kCausal>(u % sc.q_blocks) - j0;
+    j1 = len < avail ? j0 + static_cast<int>(len) : j0 + avail;
     rem = static_cast<int>(len - (j1 - j0));
   }
   __device__ bool valid() const { return j < j1; }
   __device__ bool first_step() const { return j == j0; }
-  __device__ bool last_step() const { return j == j1 - 1; }
   __device__ bool first_of_range() const { return seg_idx == 0; }
-  __device__ bool whole(int nkb) const { return j0 == 0 && j1 == nkb; }
+  __device__ bool whole(const Schedule& sc) const {
+    return j0 == 0 && j1 == sc.steps_of<kCausal>(u % sc.q_blocks);
+  }
   // Advance to the next segment (the softmax warps walk a segment with their own counter).
   __device__ void next_segment(const FwdParams& p) {
     j = j1 - 1;
@@ -179,11 +172,12 @@ struct StepCursor {
     if (++j >= j1 && rem > 0) {
       if (p.split) {
         ++u;
-        j1 = rem < p.nkb ? rem : p.nkb;
+        const int steps = p.sc.steps_of<kCausal>(u % p.sc.q_blocks);
+        j1 = rem < steps ? rem : steps;
         rem -= j1;
       } else {
         u += static_cast<int>(gridDim.x);
-        j1 = p.nkb;
+        j1 = p.sc.nkb;
         --rem;
       }
       j = j0 = 0;
@@ -205,7 +199,7 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
   // K/V blocks are re-read by every query-block pass over the same head: keep them in L2.
   const uint64_t keep = l2_policy_evict_last();
 
-  StepCursor cur;
+  StepCursor<Cfg::kCausal> cur;
   cur.init(p);
   int g = 0;  // global step index of this CTA
   int q_loaded = 0, k_issued = 0, v_issued = 0;
@@ -220,7 +214,7 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
       for (int i = 0; i < Cfg::NQ; ++i) {
         tma_load_3d(sbase + Cfg::kQOff + (b * Cfg::NQ + i) * Cfg::kTileBytes, &p.tm_q,
                     bar(Cfg::kBarQFull + b), 0,
-                    (cur.u % p.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, cur.u / p.q_blocks);
+                    (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, cur.u / p.sc.q_blocks);
       }
       q_loaded = s + 1;
     }
@@ -229,12 +223,12 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
     if (!wait_single(bar(Cfg::kBarKEmpty + st), ph ^ 1u, wd, kSiteLoadKEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarKFull + st), Cfg::kTileBytes);
     tma_load_3d_hint(sbase + Cfg::kKOff + st * Cfg::kTileBytes, &p.tm_k, bar(Cfg::kBarKFull + st),
-                     0, cur.j * Cfg::kKeys, cur.u / p.q_blocks, keep);
+                     0, cur.j * Cfg::kKeys, cur.u / p.sc.q_blocks, keep);
     k_issued = g + 1;
     if (!wait_single(bar(Cfg::kBarVEmpty + st), ph ^ 1u, wd, kSiteLoadVEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarVFull + st), Cfg::kTileBytes);
     tma_load_3d_hint(sbase + Cfg::kVOff + st * Cfg::kTileBytes, &p.tm_v, bar(Cfg::kBarVFull + st),
-                     0, cur.j * Cfg::kKeys, cur.u / p.q_blocks, keep);
+                     0, cur.j * Cfg::kKeys, cur.u / p.sc.q_blocks, keep);
     v_issued = g + 1;
     ++g;
     cur.step(p);
@@ -281,7 +275,7 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
   const bool leader = elect_one();
   bool issued_any = false;
 
-  StepCursor cs, cp;  // next S step, next P.V step
+  StepCursor<Cfg::kCausal> cs, cp;  // next S step, next P.V step
   cs.init(p);
   cp.init(p);
   int gs = 0, gp = 0;
@@ -382,7 +376,7 @@ unwind:
 template <class Cfg>
 __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, uint32_t tS,
                                              uint32_t tP, uint32_t tO, int tile, int lane, int g,
-                                             int j, bool first, float (&m_run)[2],
+                                             int j, int row0, bool first, float (&m_run)[2],
                                              float (&l_run)[2], const Watchdog& wd) {
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
   auto f = [](uint32_t u) { return __uint_as_float(u); };
@@ -396,7 +390,7 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
   __syncwarp();
   if (lane == 0) mbar_arrive(bar(Cfg::kBarSFree + tile));
 
-  if (j == p.nkb - 1) {
+  if (j == p.sc.nkb - 1) {
     // last key block of the sequence: keys past N score -inf
     const int valid = p.n - j * Cfg::kKeys;
     if (valid < Cfg::kKeys) {
@@ -406,6 +400,21 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           if (8 * i + q2 + (e & 1) >= valid) sr[4 * i + e] = __float_as_uint(-INFINITY);
+      }
+    }
+  }
+  if constexpr (Cfg::kCausal) {
+    // Keys after the query row score -inf. row0 is the first query row of this warp's 16-row
+    // slice; only blocks that reach past it need the per-element test.
+    const int key0 = j * Cfg::kKeys;
+    if (key0 + Cfg::kKeys - 1 > row0) {
+      const int t0 = row0 + (lane >> 2) - key0;  // row g: column c is masked when c > t0
+      const int q2 = 2 * (lane & 3);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (8 * i + q2 + (e & 1) > t0 + 8 * (e >> 1)) sr[4 * i + e] = __float_as_uint(-INFINITY);
       }
     }
   }
@@ -440,9 +449,16 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const float m_use = grow ? m_new[r] : m_run[r];
-    alpha[r] = ex2_approx(m_run[r] - m_use);  // 0 on a unit's first block (m_run = -inf)
+    if (Cfg::kCausal && m_use == -INFINITY) {
+      // every key so far is masked for this row (possible in a piece of a query block):
+      // O and the row sum are still zero, and p = 2^(-inf) = 0 without an -inf - -inf
+      alpha[r] = 1.0f;
+      negm2[r] = f2_splat(0.0f);
+    } else {
+      alpha[r] = ex2_approx(m_run[r] - m_use);  // 0 on a unit's first block (m_run = -inf)
+      negm2[r] = f2_splat(-m_use);
+    }
     m_run[r] = m_use;
-    negm2[r] = f2_splat(-m_use);
   }
 
   // Scale-subtract and row sums run on packed pairs (fma/add .f32x2); pair k is row k % 2.
@@ -512,14 +528,16 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
 
   int g = 0;       // global step index (phase of the per-step barriers)
   int stores = 0;  // whole units stored so far (phase of the staging barrier)
-  StepCursor cur;
+  StepCursor<Cfg::kCausal> cur;
   cur.init(p);
   while (cur.valid()) {
     float m_run[2] = {-INFINITY, -INFINITY};  // running max of s*scale*log2(e), per row
     float l_run[2] = {0.0f, 0.0f};            // this thread's partial row sums
+    const int row0 =  // first query row of this warp's slice (causal masking only)
+        Cfg::kCausal ? (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows + slice : 0;
     for (int j = cur.j0; j < cur.j1; ++j, ++g) {
-      if (!softmax_step<Cfg>(p, bars, tS, tP, tO, tile, lane, g, j, j == cur.j0, m_run, l_run,
-                             wd))
+      if (!softmax_step<Cfg>(p, bars, tS, tP, tO, tile, lane, g, j, row0, j == cur.j0, m_run,
+                             l_run, wd))
         return;
     }
     // ---- unit epilogue (g - 1 is the unit's last step)
@@ -537,7 +555,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     tmem_ld_16x256b_x8_sync(tO, o);
     tc_fence_before();
     const int b = cur.seg_idx & 1;
-    if (cur.whole(p.nkb)) {
+    if (cur.whole(p.sc)) {
       // O / l -> fp16 -> swizzled staging (this tile's slot of the unit's Q buffer) -> TMA.
       uint8_t* stage = smem + Cfg::kQOff + (b * Cfg::NQ + tile) * Cfg::kTileBytes;
 #pragma unroll
@@ -561,9 +579,9 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
         if (!wait_single(bar(Cfg::kBarStage + tile), static_cast<uint32_t>(stores) & 1u, wd,
                          kSiteSoftStage))
           return;
-        const int r0 = (cur.u % p.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
+        const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
         if (r0 < p.n) {
-          tma_store_3d(&p.tm_o, smem_addr(stage), 0, r0, cur.u / p.q_blocks);
+          tma_store_3d(&p.tm_o, smem_addr(stage), 0, r0, cur.u / p.sc.q_blocks);
           tma_store_commit();
           tma_store_wait_read();
         }
@@ -596,10 +614,10 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   }
 }
 
-template <int NQ, int STAGES>
-__global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
+template <int NQ, int STAGES, bool CAUSAL>
+__global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL>::kThreads, 1)
     mfa_fwd_kernel(const __grid_constant__ FwdParams p) {
-  using Cfg = FwdConfig<NQ, STAGES>;
+  using Cfg = FwdConfig<NQ, STAGES, CAUSAL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -667,7 +685,8 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES>::kThreads, 1)
 struct MergeParams {
   void* out;          // fp16 [BH][N][64]
   const float* workspace;
-  int n, bh, q_blocks, nkb;
+  int n;
+  Schedule sc;
   int ctas;           // grid size of the forward kernel whose pieces are merged
 };
 
@@ -680,18 +699,21 @@ struct MergeParams {
 // grid has completed and its writes are visible.
 constexpr int kMergeThreadsPerRow = 4;
 
-template <int kRowsPerUnit, int kSlotFloats>
+template <int kRowsPerUnit, int kSlotFloats, bool kCausal>
 __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
     mfa_merge_kernel(const MergeParams mp) {
   constexpr int kD = 64;
   constexpr int kChunks = kD / 4 / kMergeThreadsPerRow;  // float4 chunks per thread
   const int c = static_cast<int>(blockIdx.x);
-  const long long units = static_cast<long long>(mp.bh) * mp.q_blocks;
+  const long long total = mp.sc.total();
   long long b0, b1;
-  cta_range(units, mp.nkb, 1, c, mp.ctas, b0, b1);
-  const long long u = b1 > b0 ? (b1 - 1) / mp.nkb : 0;  // query block holding c's last step
+  split_range(total, c, mp.ctas, b0, b1);
+  int u = 0, j = 0;
+  if (b1 > b0) mp.sc.locate<kCausal>(b1 - 1, u, j);  // query block holding c's last step
+  const long long u0 = mp.sc.unit_first<kCausal>(u);
+  const long long u1 = u0 + mp.sc.steps_of<kCausal>(u % mp.sc.q_blocks);
   // Merged here only if it starts inside c and ends past it.
-  const bool mine = b1 > b0 && (u + 1) * mp.nkb > b1 && u * mp.nkb >= b0;
+  const bool mine = b1 > b0 && u1 > b1 && u0 >= b0;
   grid_dependency_wait();
   if (!mine) return;
   const int r = static_cast<int>(threadIdx.x) / kMergeThreadsPerRow;
@@ -699,13 +721,13 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   // Pieces: c's last segment (its first too if c's range starts exactly at u), then the
   // first segment of every following CTA that overlaps u.
   auto piece = [&](int cc) {
-    const int slot = cc == c ? (b0 == u * mp.nkb ? 0 : 1) : 0;
+    const int slot = cc == c ? (b0 == u0 ? 0 : 1) : 0;
     return mp.workspace + static_cast<size_t>(2 * cc + slot) * kSlotFloats;
   };
   auto overlaps = [&](int cc) {
     long long s0, s1;
-    cta_range(units, mp.nkb, 1, cc, mp.ctas, s0, s1);
-    return cc < mp.ctas && s0 < (u + 1) * mp.nkb;
+    split_range(total, cc, mp.ctas, s0, s1);
+    return cc < mp.ctas && s0 < u1;
   };
   float m_max = -INFINITY;
   for (int cc = c; overlaps(cc); ++cc) m_max = fmaxf(m_max, piece(cc)[kRowsPerUnit * kD + r]);
@@ -715,6 +737,7 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   float l = 0.0f;
   for (int cc = c; overlaps(cc); ++cc) {
     const float* ws = piece(cc);
+    // A piece whose keys are all masked for this row (causal) has m = -inf: weight 0.
     const float w = ex2_approx(ws[kRowsPerUnit * kD + r] - m_max);
     l += w * ws[kRowsPerUnit * (kD + 1) + r];
     const float4* o = reinterpret_cast<const float4*>(ws + static_cast<size_t>(r) * kD);
@@ -727,8 +750,8 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
       acc[i].w += w * v.w;
     }
   }
-  const int head = static_cast<int>(u / mp.q_blocks);
-  const int qrow = static_cast<int>(u % mp.q_blocks) * kRowsPerUnit + r;
+  const int head = u / mp.sc.q_blocks;
+  const int qrow = (u % mp.sc.q_blocks) * kRowsPerUnit + r;
   if (qrow >= mp.n) return;
   const float inv_l = 1.0f / l;
   uint2* dst = reinterpret_cast<uint2*>(static_cast<__half*>(mp.out) +

@@ -173,10 +173,6 @@ def test_errors_match_reference_messages():
     with pytest.raises(RuntimeError, match="Only N divisible by 128 and 128 is supported"):
         x = torch.zeros(1, 1, 192, 64, device="cuda", dtype=torch.float16)
         mfa.forward(x, x, x)
-    with pytest.raises(RuntimeError, match="Causal attention is not supported yet"):
-        mfa.forward(q, q, q, causal=True)
-    with pytest.raises(RuntimeError, match="Causal attention is not yet supported"):
-        mfa.forward_wmma(q, q, q, causal=True)
 
 
 def test_empty_batch():
