@@ -61,8 +61,11 @@ WORKLOADS = {
 D = 64
 
 
-def attention_flops(bh: int, n: int, d: int = D) -> float:
-    return 4.0 * bh * n * n * d
+def attention_flops(bh: int, n: int, d: int = D, causal: bool = False) -> float:
+    """4 * BH * (attended query-key pairs) * D, pairs = N^2, or N(N+1)/2 with the causal mask
+    (benchs/benchmark_forward.py:315-325)."""
+    pairs = n * (n + 1) / 2 if causal else n * n
+    return 4.0 * bh * pairs * d
 
 
 def attention_bytes(bh: int, n: int, d: int = D) -> float:
@@ -182,19 +185,19 @@ def make_inputs(wl: dict, bh: int, seed: int, device) -> tuple:
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_baseline(wl: dict, budget_s: float = 10.0) -> dict:
+def cpu_baseline(wl: dict, budget_s: float = 10.0, causal: bool = False) -> dict:
     """The reference's naive torch attention on the host cores, one head of the workload."""
     from oracle.torch_naive import torch_naive_attention
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     q, k, v = make_inputs(wl, 1, 0, "cpu")
-    flops = attention_flops(1, wl["N"])
+    flops = attention_flops(1, wl["N"], causal=causal)
     times = []
     t_end = time.perf_counter() + budget_s
     while True:
         t0 = time.perf_counter()
-        torch_naive_attention(q, k, v)
+        torch_naive_attention(q, k, v, causal=causal)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() > t_end or len(times) >= 50:
             break
@@ -272,7 +275,11 @@ def run_ours(args, wl) -> dict | None:
     n = wl["N"]
     inputs = [make_inputs(wl, bh, rank * INPUT_BUFFERS + i, dev) for i in range(INPUT_BUFFERS)]
     flush = torch.empty(L2_FLUSH_MB * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
-    fwd = mfa.forward
+    causal = args.causal
+
+    def fwd(q, k, v):
+        return mfa.forward(q, k, v, causal=causal)
+
     stream = torch.cuda.current_stream(dev)
 
     with torch.inference_mode():
@@ -310,12 +317,12 @@ def run_ours(args, wl) -> dict | None:
         e2e_steps = max(args.steps, 3)
         chunks = min(bh, E2E_CHUNKS)
         for _ in range(2):
-            mfa.forward_pinned(*host_in, out=host_out, chunks=chunks, device=dev)
+            mfa.forward_pinned(*host_in, causal=causal, out=host_out, chunks=chunks, device=dev)
         torch.cuda.synchronize(dev)
         barrier(world)
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
-            mfa.forward_pinned(*host_in, out=host_out, chunks=chunks, device=dev)
+            mfa.forward_pinned(*host_in, causal=causal, out=host_out, chunks=chunks, device=dev)
         e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
         barrier(world)
 
@@ -326,8 +333,8 @@ def run_ours(args, wl) -> dict | None:
     if rank != 0:
         return None
 
-    flops_rank_step = attention_flops(bh, n)
-    job_flops_step = attention_flops(global_bh, n)
+    flops_rank_step = attention_flops(bh, n, causal=causal)
+    job_flops_step = attention_flops(global_bh, n, causal=causal)
     value = job_flops_step * args.steps / (total_ms / 1e3) / 1e12
     kernel_ms = total_ms / args.steps
     achieved = flops_rank_step / (kernel_ms / 1e3) / 1e12
@@ -347,13 +354,13 @@ def run_ours(args, wl) -> dict | None:
         "ms_per_step": round(kernel_ms, 4),
         "higher_is_better": True,
         "scaling": wl["scaling"],
-        "vs_baseline": round(value / PUBLISHED_TFLOPS, 2),
+        "vs_baseline": None if causal else round(value / PUBLISHED_TFLOPS, 2),
         "dtype": "fp16",
         "data": "synthetic (seeded, shapes and distributions of the workload; no dataset)",
         "config": {
             "workload": args.workload,
             "B": wl["B"] * (world if wl["scaling"] == "weak" else 1), "H": wl["H"], "N": n,
-            "D": D, "bh_per_gpu": bh, "causal": False,
+            "D": D, "bh_per_gpu": bh, "causal": causal,
             "parallelism": f"batch*head sharded over {world} GPU(s), no collective",
             "l2": f"{L2_FLUSH_MB} MB write before every step, outside the timed interval",
             "input_buffers": INPUT_BUFFERS,
@@ -387,7 +394,7 @@ def run_ours(args, wl) -> dict | None:
         "wall_s_timed_region": round(wall, 4),
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(wl)
+        line["cpu_baseline"] = cpu_baseline(wl, causal=causal)
     return line
 
 
@@ -472,6 +479,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-kernel", choices=["cpu", "cute"], default="cpu")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--causal", action="store_true",
+                    help="mask key > query (flops counted over the N(N+1)/2 attended pairs)")
     ap.add_argument("--no-launch-count", action="store_true",
                     help="skip the CUPTI trace that counts launches (for runs under ncu)")
     args = ap.parse_args()
