@@ -60,6 +60,26 @@ MFA_API int mfa_fwd_f16(const void* q, const void* k, const void* v, void* out, 
 MFA_API int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, void* out, int64_t bh,
                        int64_t n, int32_t d, float scale, int32_t causal, void* stream);
 
+/* Element type and memory layout of mfa_fwd's q, k, v and out. */
+enum mfa_dtype { MFA_DTYPE_FP16 = 0, MFA_DTYPE_BF16 = 1 };
+enum mfa_layout {
+  MFA_LAYOUT_BHND = 0, /* [B, H, N, D] contiguous: the reference's layout */
+  MFA_LAYOUT_BNHD = 1  /* [B, N, H, D] contiguous: the flash-attn style layout */
+};
+
+/*
+ * General forward: `dtype` (fp16 or bf16; out has the same type), `layout` (above), B = batch
+ * and H = heads given separately. Same checks and messages as mfa_fwd_f16 (D == 64,
+ * N % 128 == 0), same causal semantics; bf16 rounds P to bf16 for the P.V product, as fp16
+ * inputs round it to fp16. No counterpart in the reference launchers, which take fp16
+ * [B*H, N, D] only; its benchmark exposes bf16 and converts to [B, N, H, D] for flash-attn
+ * (benchs/benchmark_forward.py:162-167, 188, 210-215). mfa_fwd_f16(q, k, v, out, bh, ...)
+ * equals mfa_fwd(q, k, v, out, 1, bh, ..., MFA_DTYPE_FP16, MFA_LAYOUT_BHND, stream).
+ */
+MFA_API int mfa_fwd(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                    int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
+                    int32_t dtype, int32_t layout, void* stream);
+
 /* Size of the static device scratch array used by mfa_fwd_f16_noalloc (20 MiB). */
 #define MFA_NOALLOC_SCRATCH_BYTES 20971520u
 

@@ -15,32 +15,45 @@
 
 namespace {
 
-using LaunchFn = int (*)(const void*, const void*, const void*, void*, int64_t, int64_t, int32_t,
-                         float, int32_t, void*);
+enum class Layout { kBHND, kBNHD };
 
 // flash_attn.cpp:45-75. Differences: a 3-D [B*H, N, D] view is accepted next to [B, H, N, D]
-// (same memory layout), and k / v must live on q's device.
-void check_forward_inputs(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v) {
+// (same memory layout); k / v must live on q's device; with `allow_bf16` the three tensors may
+// all be bf16 instead of fp16; the [B, N, H, D] entry point checks its own shape.
+void check_forward_inputs(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                          bool allow_bf16, Layout layout) {
   TORCH_CHECK(q.is_cuda(), "q must be a CUDA tensor");
   TORCH_CHECK(k.is_cuda(), "k must be a CUDA tensor");
   TORCH_CHECK(v.is_cuda(), "v must be a CUDA tensor");
 
-  TORCH_CHECK(q.scalar_type() == torch::kFloat16, "q must be float16");
-  TORCH_CHECK(k.scalar_type() == torch::kFloat16, "k must be float16");
-  TORCH_CHECK(v.scalar_type() == torch::kFloat16, "v must be float16");
+  if (allow_bf16) {
+    TORCH_CHECK(q.scalar_type() == torch::kFloat16 || q.scalar_type() == torch::kBFloat16,
+                "q must be float16 or bfloat16");
+    TORCH_CHECK(k.scalar_type() == q.scalar_type(), "k must have the same dtype as q");
+    TORCH_CHECK(v.scalar_type() == q.scalar_type(), "v must have the same dtype as q");
+  } else {
+    TORCH_CHECK(q.scalar_type() == torch::kFloat16, "q must be float16");
+    TORCH_CHECK(k.scalar_type() == torch::kFloat16, "k must be float16");
+    TORCH_CHECK(v.scalar_type() == torch::kFloat16, "v must be float16");
+  }
 
   TORCH_CHECK(q.is_contiguous(), "q must be contiguous");
   TORCH_CHECK(k.is_contiguous(), "k must be contiguous");
   TORCH_CHECK(v.is_contiguous(), "v must be contiguous");
 
-  TORCH_CHECK(q.dim() == 4 || q.dim() == 3, "q must have shape [B, H, N, D]");
+  if (layout == Layout::kBNHD) {
+    TORCH_CHECK(q.dim() == 4, "q must have shape [B, N, H, D]");
+  } else {
+    TORCH_CHECK(q.dim() == 4 || q.dim() == 3, "q must have shape [B, H, N, D]");
+  }
   TORCH_CHECK(k.sizes() == q.sizes(), "k must have the same shape as q");
   TORCH_CHECK(v.sizes() == q.sizes(), "v must have the same shape as q");
   TORCH_CHECK(k.device() == q.device(), "k must be on the same device as q");
   TORCH_CHECK(v.device() == q.device(), "v must be on the same device as q");
 
-  const int64_t BH = q.dim() == 4 ? q.size(0) * q.size(1) : q.size(0);
-  const int64_t N = q.size(-2);
+  const int64_t BH = q.dim() == 4 ? q.size(0) * q.size(layout == Layout::kBNHD ? 2 : 1)
+                                  : q.size(0);
+  const int64_t N = q.size(layout == Layout::kBNHD ? 1 : -2);
   const int64_t D = q.size(-1);
   TORCH_CHECK(D > 0, "D must be greater than 0");
   TORCH_CHECK(BH <= std::numeric_limits<int>::max(), "B * H is too large");
@@ -48,59 +61,84 @@ void check_forward_inputs(const torch::Tensor& q, const torch::Tensor& k, const 
   TORCH_CHECK(D <= std::numeric_limits<int>::max(), "D is too large");
 }
 
+// The (B, H, N) of q for `layout` (3-D [B*H, N, D] counts as B = 1, H = B*H).
+struct Extents {
+  int64_t batch, heads, n, d;
+};
+Extents extents_of(const torch::Tensor& q, Layout layout) {
+  if (layout == Layout::kBNHD) return {q.size(0), q.size(2), q.size(1), q.size(3)};
+  if (q.dim() == 3) return {1, q.size(0), q.size(1), q.size(2)};
+  return {q.size(0), q.size(1), q.size(2), q.size(3)};
+}
+
+void launch_general(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
+                    torch::Tensor& out, bool causal, Layout layout) {
+  const Extents e = extents_of(q, layout);
+  const float scale = 1.0f / std::sqrt(static_cast<float>(e.d));
+  const int dtype = q.scalar_type() == torch::kBFloat16 ? MFA_DTYPE_BF16 : MFA_DTYPE_FP16;
+  const int rc = mfa_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), e.batch,
+                         e.heads, e.n, static_cast<int32_t>(e.d), scale, causal ? 1 : 0, dtype,
+                         layout == Layout::kBNHD ? MFA_LAYOUT_BNHD : MFA_LAYOUT_BHND,
+                         static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
+  if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
+}
+
 // flash_attn.cpp:77-109, with empty_like instead of zeros_like: the kernel writes every
-// element of the output, so the extra memset pass of the reference is dropped.
-torch::Tensor forward_impl(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v,
-                           bool causal, LaunchFn launch) {
-  check_forward_inputs(q, k, v);
+// element of the output, so the extra memset pass of the reference is dropped. fp16 or bf16.
+torch::Tensor flash_attn_forward(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal) {
+  check_forward_inputs(q, k, v, true, Layout::kBHND);
   const c10::cuda::CUDAGuard device_guard(q.device());
   auto out = torch::empty_like(q);
+  launch_general(q, k, v, out, causal, Layout::kBHND);
+  return out;
+}
 
+// Same computation on [B, N, H, D] tensors (the flash-attn layout), output in that layout.
+torch::Tensor flash_attn_forward_bnhd(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                      bool causal) {
+  check_forward_inputs(q, k, v, true, Layout::kBNHD);
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  auto out = torch::empty_like(q);
+  launch_general(q, k, v, out, causal, Layout::kBNHD);
+  return out;
+}
+
+// The WMMA entry point keeps the reference's fp16-only contract and launcher messages.
+torch::Tensor flash_attn_forward_wmma(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                      bool causal) {
+  check_forward_inputs(q, k, v, false, Layout::kBHND);
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  auto out = torch::empty_like(q);
   const int64_t BH = q.dim() == 4 ? q.size(0) * q.size(1) : q.size(0);
   const int64_t N = q.size(-2);
   const int64_t D = q.size(-1);
   const float scale = 1.0f / std::sqrt(static_cast<float>(D));
-
-  const int rc = launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), BH, N,
-                        static_cast<int32_t>(D), scale, causal ? 1 : 0,
-                        static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
+  const int rc = mfa_fwd_simple_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), BH,
+                                    N, static_cast<int32_t>(D), scale, causal ? 1 : 0,
+                                    static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
   if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
   return out;
 }
 
-// Same as forward, writing into a caller-provided contiguous fp16 tensor of q's shape
+// Same as forward, writing into a caller-provided contiguous tensor of q's shape and dtype
 // (used by the pipelined host-buffer path to fill slices of one device buffer).
 void flash_attn_forward_into(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                              bool causal) {
-  check_forward_inputs(q, k, v);
+  check_forward_inputs(q, k, v, true, Layout::kBHND);
   TORCH_CHECK(out.is_cuda() && out.device() == q.device(), "out must be on q's device");
-  TORCH_CHECK(out.scalar_type() == torch::kFloat16, "out must be float16");
+  TORCH_CHECK(out.scalar_type() == q.scalar_type(), "out must have q's dtype");
   TORCH_CHECK(out.is_contiguous(), "out must be contiguous");
   TORCH_CHECK(out.sizes() == q.sizes(), "out must have the same shape as q");
   const c10::cuda::CUDAGuard device_guard(q.device());
-  const int64_t BH = q.dim() == 4 ? q.size(0) * q.size(1) : q.size(0);
-  const int64_t N = q.size(-2);
-  const int64_t D = q.size(-1);
-  const float scale = 1.0f / std::sqrt(static_cast<float>(D));
-  const int rc = mfa_fwd_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), BH, N,
-                             static_cast<int32_t>(D), scale, causal ? 1 : 0,
-                             static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
-  if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
-}
-
-torch::Tensor flash_attn_forward(torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal) {
-  return forward_impl(q, k, v, causal, &mfa_fwd_f16);
-}
-
-torch::Tensor flash_attn_forward_wmma(torch::Tensor q, torch::Tensor k, torch::Tensor v,
-                                      bool causal) {
-  return forward_impl(q, k, v, causal, &mfa_fwd_simple_f16);
+  launch_general(q, k, v, out, causal, Layout::kBHND);
 }
 
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward", &flash_attn_forward, "Mini Flash Attention forward (sm_100a tcgen05)");
+  m.def("forward_bnhd", &flash_attn_forward_bnhd,
+        "Mini Flash Attention forward on [B, N, H, D] tensors (fp16 or bf16)");
   m.def("forward_wmma", &flash_attn_forward_wmma,
         "Mini Flash Attention forward, single-tile sm_100a kernel (replaces the WMMA path)");
   m.def("forward_into", &flash_attn_forward_into,

@@ -31,14 +31,14 @@ __device__ int g_device_status = 0;
 
 unsigned long long g_watchdog_ns = 2000000000ull;  // 2 s per wait
 
-using FullKernel = FwdConfig<2, 3, false>;
-using FullCausal = FwdConfig<2, 3, true>;
-using SimpleKernel = FwdConfig<1, 2, false>;
-using SimpleCausal = FwdConfig<1, 2, true>;
+template <bool kCausal, bool kBF16>
+using Full = FwdConfig<2, 3, kCausal, kBF16>;
+template <bool kCausal>
+using Simple = FwdConfig<1, 2, kCausal, false>;
 
 template <class Cfg>
 cudaError_t set_smem_attribute() {
-  return cudaFuncSetAttribute(mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal>,
+  return cudaFuncSetAttribute(mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
 }
 
@@ -100,10 +100,12 @@ int prepare_device(int dev) {
       return;
     }
     e = cudaDeviceGetAttribute(&ds.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = set_smem_attribute<FullKernel>();
-    if (e == cudaSuccess) e = set_smem_attribute<FullCausal>();
-    if (e == cudaSuccess) e = set_smem_attribute<SimpleKernel>();
-    if (e == cudaSuccess) e = set_smem_attribute<SimpleCausal>();
+    if (e == cudaSuccess) e = set_smem_attribute<Full<false, false>>();
+    if (e == cudaSuccess) e = set_smem_attribute<Full<true, false>>();
+    if (e == cudaSuccess) e = set_smem_attribute<Full<false, true>>();
+    if (e == cudaSuccess) e = set_smem_attribute<Full<true, true>>();
+    if (e == cudaSuccess) e = set_smem_attribute<Simple<false>>();
+    if (e == cudaSuccess) e = set_smem_attribute<Simple<true>>();
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status_ptr), g_device_status);
     if (e == cudaSuccess) {
       // A private stream-ordered pool for the split-mode partial results: the scratch is
@@ -128,18 +130,34 @@ int prepare_device(int dev) {
   return MFA_OK;
 }
 
-int encode_bhnd(CUtensorMap* map, const void* base, int64_t n, int64_t bh) {
+// Element strides (n, h, b) of a [B, H, N, 64] (layout 0) or [B, N, H, 64] (layout 1) tensor.
+struct Strides {
+  int64_t n, h, b;
+};
+Strides layout_strides(int layout, int64_t heads, int64_t n) {
+  if (layout == MFA_LAYOUT_BNHD) return {heads * 64, 64, n * heads * 64};
+  return {64, n * 64, heads * n * 64};
+}
+
+// 4-D TMA view {64, N, H, B} of one tensor, box {64, 128, 1, 1}, 128-byte swizzle. The N
+// extent keeps tiles inside their head: rows past N read as zero and are not stored.
+int encode_tensor(CUtensorMap* map, const void* base, int64_t batch, int64_t heads, int64_t n,
+                  int layout, bool bf16) {
   std::string why;
   auto encode = tensor_map_encoder(&why);
   if (!encode) return fail(MFA_ERR_CUDA, why);
-  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(bh)};
-  const cuuint64_t strides[2] = {64 * 2, static_cast<cuuint64_t>(n) * 64 * 2};
-  const cuuint32_t box[3] = {64, 128, 1};
-  const cuuint32_t elem_strides[3] = {1, 1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
-                      strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const Strides st = layout_strides(layout, heads, n);
+  const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st.n) * 2,
+                                 static_cast<cuuint64_t>(st.h) * 2,
+                                 static_cast<cuuint64_t>(st.b) * 2};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t elem_strides[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      4, const_cast<void*>(base), dims, strides, box, elem_strides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(MFA_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
   return MFA_OK;
@@ -161,7 +179,7 @@ cudaError_t launch_merge(const MergeParams& mp, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(
-      &cfg, mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats, Cfg::kCausal>, mp);
+      &cfg, mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats, Cfg::kCausal, Cfg::kBF16>, mp);
 }
 
 // Launch plan, shared by every entry point. Persistent: one CTA per SM (or fewer for small
@@ -208,30 +226,38 @@ int plan_forward(int64_t bh, int64_t n, int64_t sms, Plan& pl) {
 // Queues the forward kernel (and the merge kernel in split mode) of plan `pl` on `stream`;
 // `workspace` holds pl.workspace_bytes.
 template <class Cfg>
-cudaError_t launch_planned(const void* q, const void* k, const void* v, void* out, int64_t bh,
-                           int64_t n, float scale, const Plan& pl, float* workspace,
-                           int* status_ptr, cudaStream_t stream, int* rc) {
+cudaError_t launch_planned(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                           int64_t heads, int64_t n, int layout, float scale, const Plan& pl,
+                           float* workspace, int* status_ptr, cudaStream_t stream, int* rc) {
   FwdParams p;
   *rc = MFA_OK;
-  if ((*rc = encode_bhnd(&p.tm_q, q, n, bh)) != MFA_OK) return cudaSuccess;
-  if ((*rc = encode_bhnd(&p.tm_k, k, n, bh)) != MFA_OK) return cudaSuccess;
-  if ((*rc = encode_bhnd(&p.tm_v, v, n, bh)) != MFA_OK) return cudaSuccess;
-  if ((*rc = encode_bhnd(&p.tm_o, out, n, bh)) != MFA_OK) return cudaSuccess;
+  const bool bf16 = Cfg::kBF16;
+  if ((*rc = encode_tensor(&p.tm_q, q, batch, heads, n, layout, bf16)) != MFA_OK) return cudaSuccess;
+  if ((*rc = encode_tensor(&p.tm_k, k, batch, heads, n, layout, bf16)) != MFA_OK) return cudaSuccess;
+  if ((*rc = encode_tensor(&p.tm_v, v, batch, heads, n, layout, bf16)) != MFA_OK) return cudaSuccess;
+  if ((*rc = encode_tensor(&p.tm_o, out, batch, heads, n, layout, bf16)) != MFA_OK)
+    return cudaSuccess;
   p.n = static_cast<int>(n);
+  p.heads = static_cast<int>(heads);
   p.sc = pl.sc;
   p.split = pl.split;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.timeout_ns = g_watchdog_ns;
   p.status = status_ptr;
   p.workspace = workspace;
-  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal>
+  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16>
       <<<static_cast<unsigned>(pl.ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && pl.split) {
+    const Strides st = layout_strides(layout, heads, n);
     MergeParams mp;
     mp.out = out;
     mp.workspace = workspace;
     mp.n = p.n;
+    mp.heads = p.heads;
+    mp.stride_b = st.b;
+    mp.stride_h = st.h;
+    mp.stride_n = st.n;
     mp.sc = pl.sc;
     mp.ctas = static_cast<int>(pl.ctas);
     e = launch_merge<Cfg>(mp, stream);
@@ -242,8 +268,9 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
 // The split plan's partial results live in a stream-ordered scratch allocation from a private
 // pool, freed on the same stream.
 template <class Cfg>
-int launch_forward(const void* q, const void* k, const void* v, void* out, int64_t bh, int64_t n,
-                   float scale, cudaStream_t stream) {
+int launch_forward(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                   int64_t heads, int64_t n, int layout, float scale, cudaStream_t stream) {
+  const int64_t bh = batch * heads;
   if (bh == 0 || n == 0) return MFA_OK;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -258,7 +285,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
                                 g_devices[dev].pool, stream);
     if (e != cudaSuccess) return fail_cuda(e, "cudaMallocFromPoolAsync (split workspace)");
   }
-  e = launch_planned<Cfg>(q, k, v, out, bh, n, scale, pl, workspace,
+  e = launch_planned<Cfg>(q, k, v, out, batch, heads, n, layout, scale, pl, workspace,
                           g_devices[dev].status_ptr, stream, &rc);
   if (pl.split) {
     const cudaError_t ef = cudaFreeAsync(workspace, stream);
@@ -322,8 +349,8 @@ int prepare_noalloc(int dev) {
       return;
     }
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = set_smem_attribute<FullKernel>();
-    if (e == cudaSuccess) e = set_smem_attribute<FullCausal>();
+    if (e == cudaSuccess) e = set_smem_attribute<Full<false, false>>();
+    if (e == cudaSuccess) e = set_smem_attribute<Full<true, false>>();
     if (e == cudaSuccess)
       e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status_ptr), g_device_status);
     if (e == cudaSuccess)
@@ -358,8 +385,8 @@ int launch_forward_noalloc(const void* q, const void* k, const void* v, void* ou
                 "mfa_fwd_f16_noalloc: this launch needs " + std::to_string(pl.workspace_bytes) +
                     " bytes of scratch, more than its static " +
                     std::to_string(MFA_NOALLOC_SCRATCH_BYTES) + "-byte array");
-  e = launch_planned<Cfg>(q, k, v, out, bh, n, scale, pl, pl.split ? st.scratch : nullptr,
-                          st.status_ptr, stream, &rc);
+  e = launch_planned<Cfg>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, pl,
+                          pl.split ? st.scratch : nullptr, st.status_ptr, stream, &rc);
   if (rc != MFA_OK) return rc;
   if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
   return MFA_OK;
@@ -408,8 +435,9 @@ extern "C" int mfa_fwd_f16(const void* q, const void* k, const void* v, void* ou
   if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return causal ? launch_forward<FullCausal>(q, k, v, out, bh, n, scale, s)
-                : launch_forward<FullKernel>(q, k, v, out, bh, n, scale, s);
+  return causal ? launch_forward<Full<true, false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s)
+                : launch_forward<Full<false, false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale,
+                                                     s);
 }
 
 extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, void* out,
@@ -424,8 +452,32 @@ extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, v
     return fail(MFA_ERR_SEQ_LEN, "Only N (seq len) divisible by 64 and 64 are supported yet");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return causal ? launch_forward<SimpleCausal>(q, k, v, out, bh, n, scale, s)
-                : launch_forward<SimpleKernel>(q, k, v, out, bh, n, scale, s);
+  return causal ? launch_forward<Simple<true>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s)
+                : launch_forward<Simple<false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s);
+}
+
+extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                       int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
+                       int32_t dtype, int32_t layout, void* stream) {
+  if (batch < 0 || heads < 0) return fail(MFA_ERR_INVALID_ARGUMENT, "negative extent");
+  if (heads > 0 && batch > 0x7fffffffLL / heads)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H is too large");
+  int rc = check_common(q, k, v, out, batch * heads, n, d);
+  if (rc != MFA_OK) return rc;
+  if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
+  if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
+  if (dtype != MFA_DTYPE_FP16 && dtype != MFA_DTYPE_BF16)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "dtype must be MFA_DTYPE_FP16 or MFA_DTYPE_BF16");
+  if (layout != MFA_LAYOUT_BHND && layout != MFA_LAYOUT_BNHD)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "layout must be MFA_LAYOUT_BHND or MFA_LAYOUT_BNHD");
+  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MFA_DTYPE_BF16)
+    return causal ? launch_forward<Full<true, true>>(q, k, v, out, batch, heads, n, layout, scale, s)
+                  : launch_forward<Full<false, true>>(q, k, v, out, batch, heads, n, layout, scale,
+                                                      s);
+  return causal ? launch_forward<Full<true, false>>(q, k, v, out, batch, heads, n, layout, scale, s)
+                : launch_forward<Full<false, false>>(q, k, v, out, batch, heads, n, layout, scale, s);
 }
 
 extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, void* out,
@@ -437,8 +489,8 @@ extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, 
   if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return causal ? launch_forward_noalloc<FullCausal>(q, k, v, out, bh, n, scale, s)
-                : launch_forward_noalloc<FullKernel>(q, k, v, out, bh, n, scale, s);
+  return causal ? launch_forward_noalloc<Full<true, false>>(q, k, v, out, bh, n, scale, s)
+                : launch_forward_noalloc<Full<false, false>>(q, k, v, out, bh, n, scale, s);
 }
 
 extern "C" const char* mfa_last_error_string(void) { return g_last_error.c_str(); }

@@ -11,11 +11,14 @@
 namespace mfa {
 
 struct FwdParams {
-  CUtensorMap tm_q;  // [BH][N][64] fp16, box 64 x 128 x 1, 128B swizzle
+  // {D=64, N, H, B} fp16 / bf16 views of q, k, v, out (box 64 x 128 x 1 x 1, 128B swizzle);
+  // the strides carry the memory layout ([B, H, N, D] or [B, N, H, D]).
+  CUtensorMap tm_q;
   CUtensorMap tm_k;
   CUtensorMap tm_v;
   CUtensorMap tm_o;
   int n;                      // sequence length (keys == queries)
+  int heads;                  // H: a (batch * head) row bh is head bh % H of batch bh / H
   Schedule sc;                // query blocks, key blocks and steps (mfa_schedule.cuh)
   // Persistent schedule. split == 0 (never with causal masking): whole query blocks, CTA c
   // takes units c, c + gridDim.x, ... . split == 1: the global steps are cut into gridDim.x

@@ -43,11 +43,12 @@
 
 namespace mfa {
 
-template <int NQ_, int STAGES_, bool CAUSAL_>
+template <int NQ_, int STAGES_, bool CAUSAL_, bool BF16_>
 struct FwdConfig {
   static constexpr int NQ = NQ_;
   static constexpr int STAGES = STAGES_;
   static constexpr bool kCausal = CAUSAL_;  // mask key index > query index
+  static constexpr bool kBF16 = BF16_;      // q, k, v, P and out in bf16 instead of fp16
   static constexpr int kRows = 128;       // query rows per tile (= MMA M)
   static constexpr int kRowsPerUnit = kRows * NQ;
   static constexpr int kKeys = 128;       // keys per block (= S tile N)
@@ -186,6 +187,15 @@ struct StepCursor {
   }
 };
 
+// Head and batch index of unit u: its (batch * head) row is u / q_blocks, heads fastest.
+struct HeadBatch {
+  int h, b;
+};
+__device__ __forceinline__ HeadBatch head_batch(const FwdParams& p, int u) {
+  const int bh = u / p.sc.q_blocks;
+  return {bh % p.heads, bh / p.heads};
+}
+
 template <class Cfg>
 __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uint32_t bars,
                                           const Watchdog& wd) {
@@ -203,8 +213,10 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
   cur.init(p);
   int g = 0;  // global step index of this CTA
   int q_loaded = 0, k_issued = 0, v_issued = 0;
+  HeadBatch hb = head_batch(p, cur.u);
   while (cur.valid()) {
     if (cur.first_step()) {
+      hb = head_batch(p, cur.u);
       const int s = cur.seg_idx, b = s & 1;
       if (!wait_single(bar(Cfg::kBarQEmpty + b), (static_cast<uint32_t>(s >> 1) & 1u) ^ 1u, wd,
                        kSiteLoadQEmpty))
@@ -212,9 +224,9 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
       mbar_arrive_expect_tx(bar(Cfg::kBarQFull + b), Cfg::NQ * Cfg::kTileBytes);
 #pragma unroll
       for (int i = 0; i < Cfg::NQ; ++i) {
-        tma_load_3d(sbase + Cfg::kQOff + (b * Cfg::NQ + i) * Cfg::kTileBytes, &p.tm_q,
+        tma_load_4d(sbase + Cfg::kQOff + (b * Cfg::NQ + i) * Cfg::kTileBytes, &p.tm_q,
                     bar(Cfg::kBarQFull + b), 0,
-                    (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, cur.u / p.sc.q_blocks);
+                    (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, hb.h, hb.b);
       }
       q_loaded = s + 1;
     }
@@ -222,13 +234,13 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
     const uint32_t ph = static_cast<uint32_t>(g / ST) & 1u;
     if (!wait_single(bar(Cfg::kBarKEmpty + st), ph ^ 1u, wd, kSiteLoadKEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarKFull + st), Cfg::kTileBytes);
-    tma_load_3d_hint(sbase + Cfg::kKOff + st * Cfg::kTileBytes, &p.tm_k, bar(Cfg::kBarKFull + st),
-                     0, cur.j * Cfg::kKeys, cur.u / p.sc.q_blocks, keep);
+    tma_load_4d_hint(sbase + Cfg::kKOff + st * Cfg::kTileBytes, &p.tm_k, bar(Cfg::kBarKFull + st),
+                     0, cur.j * Cfg::kKeys, hb.h, hb.b, keep);
     k_issued = g + 1;
     if (!wait_single(bar(Cfg::kBarVEmpty + st), ph ^ 1u, wd, kSiteLoadVEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarVFull + st), Cfg::kTileBytes);
-    tma_load_3d_hint(sbase + Cfg::kVOff + st * Cfg::kTileBytes, &p.tm_v, bar(Cfg::kBarVFull + st),
-                     0, cur.j * Cfg::kKeys, cur.u / p.sc.q_blocks, keep);
+    tma_load_4d_hint(sbase + Cfg::kVOff + st * Cfg::kTileBytes, &p.tm_v, bar(Cfg::kBarVFull + st),
+                     0, cur.j * Cfg::kKeys, hb.h, hb.b, keep);
     v_issued = g + 1;
     ++g;
     cur.step(p);
@@ -262,8 +274,8 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
   constexpr int NQ = Cfg::NQ;
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
   const uint32_t sbase = smem_addr(smem);
-  constexpr uint32_t kIdescS = idesc_f16_f32(128, 128, false);
-  constexpr uint32_t kIdescO = idesc_f16_f32(128, 64, true);
+  constexpr uint32_t kIdescS = idesc_f16_f32(128, 128, false, Cfg::kBF16);
+  constexpr uint32_t kIdescO = idesc_f16_f32(128, 64, true, Cfg::kBF16);
   // K-major Q / K tiles: SBO = 1024 (8-row swizzle atoms), LBO unused (16). MN-major V tile
   // (d contiguous): SBO = 1024 between 8-key groups, LBO = one tile (unused: the 64
   // d-columns are a single 128-byte swizzle atom).
@@ -479,7 +491,7 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
       e1 = ex2_approx(x1);
     }
     acc[k & 3] = f2_add(acc[k & 3], f2_pack(e0, e1));
-    pk[k] = pack_half2(e0, e1);
+    pk[k] = pack_pair<Cfg::kBF16>(e0, e1);
   }
   float s0, s1, t0, t1;
   f2_unpack(f2_add(acc[0], acc[2]), s0, s1);
@@ -564,8 +576,8 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
         const float inv_l = 1.0f / l_row[r];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {  // 16-byte chunk i of the row, 4 bytes per thread
-          const uint32_t w = pack_half2(__uint_as_float(o[4 * i + 2 * r]) * inv_l,
-                                        __uint_as_float(o[4 * i + 2 * r + 1]) * inv_l);
+          const uint32_t w = pack_pair<Cfg::kBF16>(__uint_as_float(o[4 * i + 2 * r]) * inv_l,
+                                                   __uint_as_float(o[4 * i + 2 * r + 1]) * inv_l);
           const uint32_t dst = smem_addr(stage + row * 128 + ((i ^ (row & 7)) << 4) + 4 * q);
           asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst), "r"(w) : "memory");
         }
@@ -581,7 +593,8 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
           return;
         const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
         if (r0 < p.n) {
-          tma_store_3d(&p.tm_o, smem_addr(stage), 0, r0, cur.u / p.sc.q_blocks);
+          const HeadBatch ob = head_batch(p, cur.u);
+          tma_store_4d(&p.tm_o, smem_addr(stage), 0, r0, ob.h, ob.b);
           tma_store_commit();
           tma_store_wait_read();
         }
@@ -614,10 +627,10 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   }
 }
 
-template <int NQ, int STAGES, bool CAUSAL>
-__global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL>::kThreads, 1)
+template <int NQ, int STAGES, bool CAUSAL, bool BF16>
+__global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16>::kThreads, 1)
     mfa_fwd_kernel(const __grid_constant__ FwdParams p) {
-  using Cfg = FwdConfig<NQ, STAGES, CAUSAL>;
+  using Cfg = FwdConfig<NQ, STAGES, CAUSAL, BF16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -683,9 +696,11 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL>::kThreads, 1)
 
 // ---------------------------------------------------------------- split-mode merge
 struct MergeParams {
-  void* out;          // fp16 [BH][N][64]
+  void* out;          // fp16 / bf16, row (b, h, n) at b * stride_b + h * stride_h + n * stride_n
   const float* workspace;
   int n;
+  int heads;
+  long long stride_b, stride_h, stride_n;  // in elements
   Schedule sc;
   int ctas;           // grid size of the forward kernel whose pieces are merged
 };
@@ -699,7 +714,7 @@ struct MergeParams {
 // grid has completed and its writes are visible.
 constexpr int kMergeThreadsPerRow = 4;
 
-template <int kRowsPerUnit, int kSlotFloats, bool kCausal>
+template <int kRowsPerUnit, int kSlotFloats, bool kCausal, bool kBF16>
 __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
     mfa_merge_kernel(const MergeParams mp) {
   constexpr int kD = 64;
@@ -750,17 +765,19 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
       acc[i].w += w * v.w;
     }
   }
-  const int head = u / mp.sc.q_blocks;
+  const int bh = u / mp.sc.q_blocks;
   const int qrow = (u % mp.sc.q_blocks) * kRowsPerUnit + r;
   if (qrow >= mp.n) return;
   const float inv_l = 1.0f / l;
-  uint2* dst = reinterpret_cast<uint2*>(static_cast<__half*>(mp.out) +
-                                        (static_cast<size_t>(head) * mp.n + qrow) * kD);
+  const long long offset = static_cast<long long>(bh / mp.heads) * mp.stride_b +
+                           static_cast<long long>(bh % mp.heads) * mp.stride_h +
+                           static_cast<long long>(qrow) * mp.stride_n;
+  uint2* dst = reinterpret_cast<uint2*>(static_cast<uint16_t*>(mp.out) + offset);
 #pragma unroll
   for (int i = 0; i < kChunks; ++i) {
     uint2 w;
-    w.x = pack_half2(acc[i].x * inv_l, acc[i].y * inv_l);
-    w.y = pack_half2(acc[i].z * inv_l, acc[i].w * inv_l);
+    w.x = pack_pair<kBF16>(acc[i].x * inv_l, acc[i].y * inv_l);
+    w.y = pack_pair<kBF16>(acc[i].z * inv_l, acc[i].w * inv_l);
     dst[kMergeThreadsPerRow * i + k] = w;
   }
 }

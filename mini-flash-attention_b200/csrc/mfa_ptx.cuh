@@ -103,6 +103,36 @@ __device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void* tmap,
       : "memory");
 }
 
+// 4-D tiled loads / store: coordinates {d, row, head, batch} of a {D, N, H, B} tensor map.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
+                                            int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const void* tmap, uint32_t bar,
+                                                 int c0, int c1, int c2, int c3,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
@@ -385,9 +415,12 @@ __device__ __forceinline__ uint64_t desc_join(uint32_t lo, uint32_t hi) {
 // Instruction descriptor for kind::f16 with fp16 A/B and fp32 accumulation.
 // bits 4-5 D format (1 = f32), 7-9 A format (0 = f16), 10-12 B format (0 = f16),
 // bit 15 A major (0 = K), bit 16 B major (1 = MN), 17-22 N>>3, 24-28 M>>4.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool b_mn_major) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | ((b_mn_major ? 1u : 0u) << 16) |
-         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool b_mn_major,
+                                                     bool bf16 = false) {
+  // A and B are both fp16 (format 0) or both bf16 (format 1): one kind::f16 MMA never mixes.
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (0u << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]
@@ -470,6 +503,18 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// fp16 or bf16 pair, low half first.
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
+  return kBF16 ? pack_bf162(lo, hi) : pack_half2(lo, hi);
 }
 
 }  // namespace mfa

@@ -1,13 +1,15 @@
 """mini-flash-attention for B200 (sm_100a).
 
 Drop-in for the reference package's public API (src/mini_flash_attention/__init__.py:1-3):
-``forward`` and ``forward_wmma`` take fp16 q, k, v of shape [B, H, N, D] (or [B*H, N, D]),
-D = 64, and return softmax(q k^T / sqrt(D)) v as fp16, computed by hand-written tcgen05
-kernels. There is no CPU or Triton fallback: without the built sm_100a extension the calls
-raise.
+``forward`` and ``forward_wmma`` take q, k, v of shape [B, H, N, D] (or [B*H, N, D]), D = 64,
+and return softmax(q k^T / sqrt(D)) v, computed by hand-written tcgen05 kernels; ``causal=True``
+masks key index > query index. ``forward`` takes fp16 or bf16, ``forward_wmma`` fp16 (the
+reference's contract). There is no CPU or Triton fallback: without the built sm_100a extension
+the calls raise.
+``forward_bnhd`` is ``forward`` on [B, N, H, D] tensors (the flash-attn layout).
 ``forward_pinned`` runs the same forward on host tensors, overlapping the host<->device
 copies of batch*head slices with the kernels.
 """
-from ._cuda import forward, forward_pinned, forward_wmma
+from ._cuda import forward, forward_bnhd, forward_pinned, forward_wmma
 
-__all__ = ["forward", "forward_wmma", "forward_pinned"]
+__all__ = ["forward", "forward_wmma", "forward_bnhd", "forward_pinned"]

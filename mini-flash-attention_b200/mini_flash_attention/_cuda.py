@@ -34,7 +34,15 @@ def _load_extension():
 
 
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False) -> torch.Tensor:
+    """softmax(q k^T / sqrt(D)) v on [B, H, N, D] (or [B*H, N, D]) tensors, fp16 or bf16;
+    causal=True masks key index > query index."""
     return _load_extension().forward(q, k, v, causal)
+
+
+def forward_bnhd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                 causal: bool = False) -> torch.Tensor:
+    """forward on [B, N, H, D] tensors (the flash-attn layout); the output has that layout."""
+    return _load_extension().forward_bnhd(q, k, v, causal)
 
 
 def forward_wmma(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False) -> torch.Tensor:

@@ -15,6 +15,7 @@ EXPORTED_SYMBOLS = (
     "mfa_fwd_f16",
     "mfa_fwd_simple_f16",
     "mfa_fwd_f16_noalloc",
+    "mfa_fwd",
     "mfa_last_error_string",
     "mfa_device_status",
     "mfa_set_watchdog_ns",
@@ -31,6 +32,8 @@ MFA_ERR_CUDA = 5
 MFA_ERR_DEVICE = 6
 STATUS_TIMEOUT_BASE = 0x100
 NOALLOC_SCRATCH_BYTES = 20971520  # MFA_NOALLOC_SCRATCH_BYTES
+DTYPE_FP16, DTYPE_BF16 = 0, 1
+LAYOUT_BHND, LAYOUT_BNHD = 0, 1
 
 _LIB: ctypes.CDLL | None = None
 
@@ -54,6 +57,11 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = fwd_args
         fn.restype = ctypes.c_int
+    lib.mfa_fwd.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                    ctypes.c_int32, ctypes.c_float, ctypes.c_int32,
+                                                    ctypes.c_int32, ctypes.c_int32,
+                                                    ctypes.c_void_p]
+    lib.mfa_fwd.restype = ctypes.c_int
     lib.mfa_last_error_string.argtypes = []
     lib.mfa_last_error_string.restype = ctypes.c_char_p
     lib.mfa_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
@@ -93,6 +101,14 @@ def fwd_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, bh: int, n: in
     on a device, so calls must not overlap on the GPU); raises MfaError."""
     _check(load().mfa_fwd_f16_noalloc(q_ptr, k_ptr, v_ptr, out_ptr, bh, n, d, scale,
                                        int(causal), stream))
+
+
+def fwd_general(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, heads: int,
+                n: int, d: int, scale: float, causal: bool = False, dtype: int = DTYPE_FP16,
+                layout: int = LAYOUT_BHND, stream: int = 0) -> None:
+    """Launch mfa_fwd (dtype and layout selectable); raises MfaError."""
+    _check(load().mfa_fwd(q_ptr, k_ptr, v_ptr, out_ptr, batch, heads, n, d, scale, int(causal),
+                          dtype, layout, stream))
 
 
 def device_status(device: int = 0, reset: bool = True) -> int:

@@ -8,7 +8,7 @@ import torch
 import mini_flash_attention as mfa
 
 
-@pytest.mark.parametrize("fn", [mfa.forward, mfa.forward_wmma])
+@pytest.mark.parametrize("fn", [mfa.forward, mfa.forward_wmma, mfa.forward_bnhd])
 def test_cpu_tensors_rejected(fn):
     q = torch.randn(1, 2, 128, 64, dtype=torch.float16)
     with pytest.raises(RuntimeError, match="q must be a CUDA tensor"):
@@ -18,7 +18,7 @@ def test_cpu_tensors_rejected(fn):
 def test_public_signature_matches_reference():
     import inspect
 
-    for fn in (mfa.forward, mfa.forward_wmma):
+    for fn in (mfa.forward, mfa.forward_wmma, mfa.forward_bnhd):
         params = inspect.signature(fn).parameters
         assert list(params) == ["q", "k", "v", "causal"]
         assert params["causal"].default is False

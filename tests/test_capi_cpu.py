@@ -117,3 +117,24 @@ def test_watchdog_limit_validated():
         capi.set_watchdog_ns(10)
     assert e.value.code == capi.MFA_ERR_INVALID_ARGUMENT
     capi.set_watchdog_ns(2_000_000_000)
+
+
+def test_general_entry_validates_dtype_layout_and_shape():
+    def call(**kw):
+        args = dict(batch=2, heads=3, n=256, d=64, scale=0.125, dtype=capi.DTYPE_BF16,
+                    layout=capi.LAYOUT_BNHD)
+        args.update(kw)
+        with pytest.raises(capi.MfaError) as e:
+            capi.fwd_general(FAKE, FAKE, FAKE, FAKE, **args)
+        return e.value
+    assert call(dtype=7).code == capi.MFA_ERR_INVALID_ARGUMENT
+    assert call(layout=5).code == capi.MFA_ERR_INVALID_ARGUMENT
+    e = call(d=128)
+    assert (e.code, str(e)) == (capi.MFA_ERR_HEAD_DIM, "This kernel supports only D=64")
+    e = call(n=200)
+    assert (e.code, str(e)) == (capi.MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported")
+    assert call(batch=-1).code == capi.MFA_ERR_INVALID_ARGUMENT
+    # valid arguments reach the device (no GPU here)
+    assert call().code in (capi.MFA_ERR_CUDA, capi.MFA_ERR_DEVICE)
+    # empty problems are no-ops
+    capi.fwd_general(FAKE, FAKE, FAKE, FAKE, 0, 3, 256, 64, 0.125)

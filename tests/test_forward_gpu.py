@@ -152,11 +152,18 @@ def test_non_default_device_guard():
     torch.testing.assert_close(out.float(), naive_fp32(q, k, v), atol=ATOL_NAIVE, rtol=RTOL_NAIVE)
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_wrong_dtype_rejected(dtype):
-    q = torch.zeros(1, 1, 128, 64, device="cuda", dtype=dtype)
+def test_wrong_dtype_rejected():
+    q = torch.zeros(1, 1, 128, 64, device="cuda", dtype=torch.float32)
     with pytest.raises(RuntimeError, match="q must be float16"):
         mfa.forward(q, q, q)
+    with pytest.raises(RuntimeError, match="q must be float16"):
+        mfa.forward_wmma(q, q, q)
+    # forward also takes bf16; the WMMA entry point keeps the reference's fp16-only contract
+    b = q.bfloat16()
+    with pytest.raises(RuntimeError, match="q must be float16"):
+        mfa.forward_wmma(b, b, b)
+    with pytest.raises(RuntimeError, match="k must have the same dtype as q"):
+        mfa.forward(b, q.half(), b)
 
 
 def test_errors_match_reference_messages():
