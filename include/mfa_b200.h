@@ -30,7 +30,7 @@ enum mfa_status_code {
   MFA_OK = 0,
   MFA_ERR_INVALID_ARGUMENT = 1, /* null / misaligned pointer, negative or oversized extent */
   MFA_ERR_HEAD_DIM = 2,         /* D != 64 */
-  MFA_ERR_SEQ_LEN = 3,          /* N not a multiple of the entry point's block size */
+  MFA_ERR_SEQ_LEN = 3,          /* N not a multiple of 64 (mfa_fwd_simple_f16 only) */
   MFA_ERR_CAUSAL = 4,           /* reserved: causal masking is supported by every entry point */
   MFA_ERR_CUDA = 5,             /* CUDA runtime or driver error; message has the details */
   MFA_ERR_DEVICE = 6            /* current device is not an sm_100 (B200-class) GPU */
@@ -39,9 +39,11 @@ enum mfa_status_code {
 /*
  * Attention forward, tcgen05 kernel with two query tiles (256 rows) per CTA.
  * Replaces the reference launcher launch_flash_attn_forward
- * (src/mini_flash_attention/flash_attn_cuda.cu:370-420): same arguments, the same D == 64 and
- * N % 128 == 0 checks in the same order with the same messages. `scale` multiplies q.k before
- * the softmax (the reference binding passes 1/sqrt(D), flash_attn.cpp:94). causal != 0 masks
+ * (src/mini_flash_attention/flash_attn_cuda.cu:370-420): same arguments, the same D == 64 check
+ * and message; any N >= 1 (the reference requires N % 128 == 0, flash_attn_cuda.cu:402-407).
+ * `scale` multiplies q.k before the softmax (the reference binding passes 1/sqrt(D),
+ * flash_attn.cpp:94). q, k, v and out must be memory of the current device (checked: other
+ * pointers return MFA_ERR_INVALID_ARGUMENT before any launch). causal != 0 masks
  * key index > query index (the reference launcher rejects causal, flash_attn_cuda.cu:408-410;
  * the mask is the one its test and benchmark build, tests/test_forward.py:30-32).
  * bh == 0 or n == 0 is a no-op that returns MFA_OK.
@@ -69,8 +71,8 @@ enum mfa_layout {
 
 /*
  * General forward: `dtype` (fp16 or bf16; out has the same type), `layout` (above), B = batch
- * and H = heads given separately. Same checks and messages as mfa_fwd_f16 (D == 64,
- * N % 128 == 0), same causal semantics; bf16 rounds P to bf16 for the P.V product, as fp16
+ * and H = heads given separately. Same checks and messages as mfa_fwd_f16 (D == 64, any N),
+ * same causal semantics; bf16 rounds P to bf16 for the P.V product, as fp16
  * inputs round it to fp16. No counterpart in the reference launchers, which take fp16
  * [B*H, N, D] only; its benchmark exposes bf16 and converts to [B, N, H, D] for flash-attn
  * (benchs/benchmark_forward.py:162-167, 188, 210-215). mfa_fwd_f16(q, k, v, out, bh, ...)

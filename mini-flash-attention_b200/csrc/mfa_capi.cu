@@ -57,6 +57,8 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
+int check_device_pointers(const void* q, const void* k, const void* v, const void* out, int dev);
+
 int fail_cuda(cudaError_t e, const char* what) {
   return fail(MFA_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(e) + " (" + what + ")");
 }
@@ -277,6 +279,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
   int rc = prepare_device(dev);
   if (rc != MFA_OK) return rc;
+  if ((rc = check_device_pointers(q, k, v, out, dev)) != MFA_OK) return rc;
   Plan pl;
   if ((rc = plan_forward<Cfg>(bh, n, g_devices[dev].num_sms, pl)) != MFA_OK) return rc;
   float* workspace = nullptr;
@@ -307,6 +310,28 @@ int check_common(const void* q, const void* k, const void* v, void* out, int64_t
                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
   if (any & 15u)
     return fail(MFA_ERR_INVALID_ARGUMENT, "q, k, v and out must be 16-byte aligned");
+  return MFA_OK;
+}
+
+// q, k, v and out must be memory that device `dev` addresses directly (its own device memory
+// or managed memory). A host, foreign or dangling pointer is refused here, before anything is
+// launched, instead of faulting the GPU inside the kernel.
+int check_device_pointers(const void* q, const void* k, const void* v, const void* out, int dev) {
+  const void* ptrs[4] = {q, k, v, out};
+  const char* names[4] = {"q", "k", "v", "out"};
+  for (int i = 0; i < 4; ++i) {
+    cudaPointerAttributes a = {};
+    const cudaError_t e = cudaPointerGetAttributes(&a, ptrs[i]);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(MFA_ERR_INVALID_ARGUMENT, std::string(names[i]) + " is not a CUDA pointer");
+    }
+    const bool ok = (a.type == cudaMemoryTypeDevice && a.device == dev) ||
+                    a.type == cudaMemoryTypeManaged;
+    if (!ok)
+      return fail(MFA_ERR_INVALID_ARGUMENT,
+                  std::string(names[i]) + " must point to memory of the current device");
+  }
   return MFA_OK;
 }
 
@@ -375,6 +400,7 @@ int launch_forward_noalloc(const void* q, const void* k, const void* v, void* ou
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
   int rc = prepare_noalloc(dev);
   if (rc != MFA_OK) return rc;
+  if ((rc = check_device_pointers(q, k, v, out, dev)) != MFA_OK) return rc;
   const NoAllocState& st = g_noalloc[dev];
   Plan pl;
   if ((rc = plan_forward<Cfg>(bh, n, st.num_sms, pl)) != MFA_OK) return rc;
@@ -429,10 +455,11 @@ extern "C" int mfa_fwd_f16(const void* q, const void* k, const void* v, void* ou
                            int64_t n, int32_t d, float scale, int32_t causal, void* stream) {
   int rc = check_common(q, k, v, out, bh, n, d);
   if (rc != MFA_OK) return rc;
-  // The D and N checks and messages of flash_attn_cuda.cu:399-407, in that order. Causal
-  // masking (rejected by flash_attn_cuda.cu:408-410) is supported.
+  // The D check and message of flash_attn_cuda.cu:399-401. Any N is supported (the reference
+  // requires N % 128 == 0, flash_attn_cuda.cu:402-407: here the TMA maps zero-fill rows past N,
+  // the last key block masks keys past N and the stores clip rows past N), and so is causal
+  // masking (rejected by flash_attn_cuda.cu:408-410).
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
-  if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return causal ? launch_forward<Full<true, false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s)
@@ -465,7 +492,6 @@ extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, i
   int rc = check_common(q, k, v, out, batch * heads, n, d);
   if (rc != MFA_OK) return rc;
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
-  if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
   if (dtype != MFA_DTYPE_FP16 && dtype != MFA_DTYPE_BF16)
     return fail(MFA_ERR_INVALID_ARGUMENT, "dtype must be MFA_DTYPE_FP16 or MFA_DTYPE_BF16");
   if (layout != MFA_LAYOUT_BHND && layout != MFA_LAYOUT_BNHD)
@@ -486,7 +512,6 @@ extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, 
   int rc = check_common(q, k, v, out, bh, n, d);
   if (rc != MFA_OK) return rc;
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
-  if (n % 128 != 0) return fail(MFA_ERR_SEQ_LEN, "Only N divisible by 128 and 128 is supported");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return causal ? launch_forward_noalloc<Full<true, false>>(q, k, v, out, bh, n, scale, s)

@@ -177,9 +177,9 @@ def test_errors_match_reference_messages():
     with pytest.raises(RuntimeError, match="This kernel supports only D=64"):
         x = torch.zeros(1, 1, 128, 32, device="cuda", dtype=torch.float16)
         mfa.forward(x, x, x)
-    with pytest.raises(RuntimeError, match="Only N divisible by 128 and 128 is supported"):
-        x = torch.zeros(1, 1, 192, 64, device="cuda", dtype=torch.float16)
-        mfa.forward(x, x, x)
+    with pytest.raises(RuntimeError, match="Only N \\(seq len\\) divisible by 64 and 64"):
+        x = torch.zeros(1, 1, 96, 64, device="cuda", dtype=torch.float16)
+        mfa.forward_wmma(x, x, x)
 
 
 def test_empty_batch():

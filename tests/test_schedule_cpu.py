@@ -143,7 +143,8 @@ def merge_plan(sc, c, ctas):
 CASES = [(8, 8192, 256, 148), (1, 128, 256, 148), (2, 2048, 256, 148), (256, 4096, 256, 148),
          (2048, 512, 256, 148), (3, 192, 128, 148), (6, 256, 256, 148),
          (7, 1024, 256, 13), (5, 640, 128, 148), (1, 4096, 256, 148), (3, 384, 256, 148),
-         (2, 1152, 256, 148), (4, 2304, 128, 37)]
+         (2, 1152, 256, 148), (4, 2304, 128, 37), (3, 300, 256, 148), (1, 1, 256, 148),
+         (5, 1000, 256, 148), (2, 4095, 256, 148), (7, 77, 256, 13)]
 
 
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])

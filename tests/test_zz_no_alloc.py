@@ -50,7 +50,8 @@ def test_noalloc_matches_forward_on_two_calls_in_a_row():
 
 
 def test_noalloc_rejects_bad_arguments_like_forward():
+    # fails argument validation before any device work (the pointers are never used)
     with pytest.raises(capi.MfaError) as e:
-        capi.fwd_noalloc(0x10000, 0x10000, 0x10000, 0x10000, 2, 192, D, 0.125)
-    assert e.value.code == capi.MFA_ERR_SEQ_LEN
-    assert str(e.value) == "Only N divisible by 128 and 128 is supported"
+        capi.fwd_noalloc(0x10000, 0x10000, 0x10000, 0x10000, 2, 256, 32, 0.125)
+    assert e.value.code == capi.MFA_ERR_HEAD_DIM
+    assert str(e.value) == "This kernel supports only D=64"
