@@ -29,7 +29,7 @@ extern "C" {
 enum mfa_status_code {
   MFA_OK = 0,
   MFA_ERR_INVALID_ARGUMENT = 1, /* null / misaligned pointer, negative or oversized extent */
-  MFA_ERR_HEAD_DIM = 2,         /* D != 64 */
+  MFA_ERR_HEAD_DIM = 2,         /* unsupported D (64 only, or 32 / 64 / 128 for mfa_fwd) */
   MFA_ERR_SEQ_LEN = 3,          /* N not a multiple of 64 (mfa_fwd_simple_f16 only) */
   MFA_ERR_CAUSAL = 4,           /* reserved: causal masking is supported by every entry point */
   MFA_ERR_CUDA = 5,             /* CUDA runtime or driver error; message has the details */
@@ -71,8 +71,8 @@ enum mfa_layout {
 
 /*
  * General forward: `dtype` (fp16 or bf16; out has the same type), `layout` (above), B = batch
- * and H = heads given separately. Same checks and messages as mfa_fwd_f16 (D == 64, any N),
- * same causal semantics; bf16 rounds P to bf16 for the P.V product, as fp16
+ * and H = heads given separately, head dim d = 32, 64 or 128 (others: MFA_ERR_HEAD_DIM, "This
+ * kernel supports only D=32, D=64 and D=128"), any N, same causal semantics as mfa_fwd_f16; bf16 rounds P to bf16 for the P.V product, as fp16
  * inputs round it to fp16. No counterpart in the reference launchers, which take fp16
  * [B*H, N, D] only; its benchmark exposes bf16 and converts to [B, N, H, D] for flash-attn
  * (benchs/benchmark_forward.py:162-167, 188, 210-215). mfa_fwd_f16(q, k, v, out, bh, ...)

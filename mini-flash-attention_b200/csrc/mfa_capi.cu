@@ -31,15 +31,27 @@ __device__ int g_device_status = 0;
 
 unsigned long long g_watchdog_ns = 2000000000ull;  // 2 s per wait
 
-template <bool kCausal, bool kBF16>
-using Full = FwdConfig<2, 3, kCausal, kBF16>;
+// Two 128-row query tiles per CTA and a 3-slot K/V ring, except for D = 128, whose O would
+// not fit twice in TMEM next to S and P: one tile per CTA and a 2-slot ring (shared memory).
+template <bool kCausal, bool kBF16, int D = 64>
+using Full = FwdConfig<D == 128 ? 1 : 2, D == 128 ? 2 : 3, kCausal, kBF16, D>;
 template <bool kCausal>
-using Simple = FwdConfig<1, 2, kCausal, false>;
+using Simple = FwdConfig<1, 2, kCausal, false, 64>;
 
 template <class Cfg>
 cudaError_t set_smem_attribute() {
-  return cudaFuncSetAttribute(mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  return cudaFuncSetAttribute(
+      mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim>,
+      cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+}
+
+template <int D>
+cudaError_t set_smem_attributes_d() {
+  cudaError_t e = set_smem_attribute<Full<false, false, D>>();
+  if (e == cudaSuccess) e = set_smem_attribute<Full<true, false, D>>();
+  if (e == cudaSuccess) e = set_smem_attribute<Full<false, true, D>>();
+  if (e == cudaSuccess) e = set_smem_attribute<Full<true, true, D>>();
+  return e;
 }
 
 struct DeviceState {
@@ -102,10 +114,9 @@ int prepare_device(int dev) {
       return;
     }
     e = cudaDeviceGetAttribute(&ds.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = set_smem_attribute<Full<false, false>>();
-    if (e == cudaSuccess) e = set_smem_attribute<Full<true, false>>();
-    if (e == cudaSuccess) e = set_smem_attribute<Full<false, true>>();
-    if (e == cudaSuccess) e = set_smem_attribute<Full<true, true>>();
+    if (e == cudaSuccess) e = set_smem_attributes_d<32>();
+    if (e == cudaSuccess) e = set_smem_attributes_d<64>();
+    if (e == cudaSuccess) e = set_smem_attributes_d<128>();
     if (e == cudaSuccess) e = set_smem_attribute<Simple<false>>();
     if (e == cudaSuccess) e = set_smem_attribute<Simple<true>>();
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status_ptr), g_device_status);
@@ -132,33 +143,36 @@ int prepare_device(int dev) {
   return MFA_OK;
 }
 
-// Element strides (n, h, b) of a [B, H, N, 64] (layout 0) or [B, N, H, 64] (layout 1) tensor.
+// Element strides (n, h, b) of a [B, H, N, D] (layout 0) or [B, N, H, D] (layout 1) tensor.
 struct Strides {
   int64_t n, h, b;
 };
-Strides layout_strides(int layout, int64_t heads, int64_t n) {
-  if (layout == MFA_LAYOUT_BNHD) return {heads * 64, 64, n * heads * 64};
-  return {64, n * 64, heads * n * 64};
+Strides layout_strides(int layout, int64_t heads, int64_t n, int64_t d) {
+  if (layout == MFA_LAYOUT_BNHD) return {heads * d, d, n * heads * d};
+  return {d, n * d, heads * n * d};
 }
 
-// 4-D TMA view {64, N, H, B} of one tensor, box {64, 128, 1, 1}, 128-byte swizzle. The N
-// extent keeps tiles inside their head: rows past N read as zero and are not stored.
+// 4-D TMA view {D, N, H, B} of one tensor, box {min(D, 64), 128, 1, 1}: 128-byte swizzle for
+// 64-column boxes, 64-byte swizzle for D = 32. The N extent keeps tiles inside their head:
+// rows past N read as zero and are not stored.
 int encode_tensor(CUtensorMap* map, const void* base, int64_t batch, int64_t heads, int64_t n,
-                  int layout, bool bf16) {
+                  int64_t d, int layout, bool bf16) {
   std::string why;
   auto encode = tensor_map_encoder(&why);
   if (!encode) return fail(MFA_ERR_CUDA, why);
-  const Strides st = layout_strides(layout, heads, n);
-  const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(heads),
-                              static_cast<cuuint64_t>(batch)};
+  const Strides st = layout_strides(layout, heads, n, d);
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(n),
+                              static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
   const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st.n) * 2,
                                  static_cast<cuuint64_t>(st.h) * 2,
                                  static_cast<cuuint64_t>(st.b) * 2};
-  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t box_cols = d < 64 ? static_cast<cuuint32_t>(d) : 64;
+  const cuuint32_t box[4] = {box_cols, 128, 1, 1};
   const cuuint32_t elem_strides[4] = {1, 1, 1, 1};
   CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                       4, const_cast<void*>(base), dims, strides, box, elem_strides,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(MFA_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
@@ -180,8 +194,10 @@ cudaError_t launch_merge(const MergeParams& mp, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(
-      &cfg, mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats, Cfg::kCausal, Cfg::kBF16>, mp);
+  return cudaLaunchKernelEx(&cfg,
+                            mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats, Cfg::kCausal,
+                                             Cfg::kBF16, Cfg::kHeadDim>,
+                            mp);
 }
 
 // Launch plan, shared by every entry point. Persistent: one CTA per SM (or fewer for small
@@ -234,10 +250,14 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
   FwdParams p;
   *rc = MFA_OK;
   const bool bf16 = Cfg::kBF16;
-  if ((*rc = encode_tensor(&p.tm_q, q, batch, heads, n, layout, bf16)) != MFA_OK) return cudaSuccess;
-  if ((*rc = encode_tensor(&p.tm_k, k, batch, heads, n, layout, bf16)) != MFA_OK) return cudaSuccess;
-  if ((*rc = encode_tensor(&p.tm_v, v, batch, heads, n, layout, bf16)) != MFA_OK) return cudaSuccess;
-  if ((*rc = encode_tensor(&p.tm_o, out, batch, heads, n, layout, bf16)) != MFA_OK)
+  const int64_t d = Cfg::kHeadDim;
+  if ((*rc = encode_tensor(&p.tm_q, q, batch, heads, n, d, layout, bf16)) != MFA_OK)
+    return cudaSuccess;
+  if ((*rc = encode_tensor(&p.tm_k, k, batch, heads, n, d, layout, bf16)) != MFA_OK)
+    return cudaSuccess;
+  if ((*rc = encode_tensor(&p.tm_v, v, batch, heads, n, d, layout, bf16)) != MFA_OK)
+    return cudaSuccess;
+  if ((*rc = encode_tensor(&p.tm_o, out, batch, heads, n, d, layout, bf16)) != MFA_OK)
     return cudaSuccess;
   p.n = static_cast<int>(n);
   p.heads = static_cast<int>(heads);
@@ -247,11 +267,11 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
   p.timeout_ns = g_watchdog_ns;
   p.status = status_ptr;
   p.workspace = workspace;
-  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16>
+  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim>
       <<<static_cast<unsigned>(pl.ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && pl.split) {
-    const Strides st = layout_strides(layout, heads, n);
+    const Strides st = layout_strides(layout, heads, n, d);
     MergeParams mp;
     mp.out = out;
     mp.workspace = workspace;
@@ -483,6 +503,25 @@ extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, v
                 : launch_forward<Simple<false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s);
 }
 
+namespace mfa {
+namespace {
+template <int D>
+int launch_general(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                   int64_t heads, int64_t n, float scale, int32_t causal, int32_t dtype,
+                   int32_t layout, cudaStream_t s) {
+  if (dtype == MFA_DTYPE_BF16)
+    return causal ? launch_forward<Full<true, true, D>>(q, k, v, out, batch, heads, n, layout,
+                                                        scale, s)
+                  : launch_forward<Full<false, true, D>>(q, k, v, out, batch, heads, n, layout,
+                                                         scale, s);
+  return causal ? launch_forward<Full<true, false, D>>(q, k, v, out, batch, heads, n, layout,
+                                                       scale, s)
+                : launch_forward<Full<false, false, D>>(q, k, v, out, batch, heads, n, layout,
+                                                        scale, s);
+}
+}  // namespace
+}  // namespace mfa
+
 extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, int64_t batch,
                        int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
                        int32_t dtype, int32_t layout, void* stream) {
@@ -491,19 +530,18 @@ extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, i
     return fail(MFA_ERR_INVALID_ARGUMENT, "B * H is too large");
   int rc = check_common(q, k, v, out, batch * heads, n, d);
   if (rc != MFA_OK) return rc;
-  if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
+  if (d != 32 && d != 64 && d != 128)
+    return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=32, D=64 and D=128");
   if (dtype != MFA_DTYPE_FP16 && dtype != MFA_DTYPE_BF16)
     return fail(MFA_ERR_INVALID_ARGUMENT, "dtype must be MFA_DTYPE_FP16 or MFA_DTYPE_BF16");
   if (layout != MFA_LAYOUT_BHND && layout != MFA_LAYOUT_BNHD)
     return fail(MFA_ERR_INVALID_ARGUMENT, "layout must be MFA_LAYOUT_BHND or MFA_LAYOUT_BNHD");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == MFA_DTYPE_BF16)
-    return causal ? launch_forward<Full<true, true>>(q, k, v, out, batch, heads, n, layout, scale, s)
-                  : launch_forward<Full<false, true>>(q, k, v, out, batch, heads, n, layout, scale,
-                                                      s);
-  return causal ? launch_forward<Full<true, false>>(q, k, v, out, batch, heads, n, layout, scale, s)
-                : launch_forward<Full<false, false>>(q, k, v, out, batch, heads, n, layout, scale, s);
+  if (d == 32) return launch_general<32>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s);
+  if (d == 128)
+    return launch_general<128>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s);
+  return launch_general<64>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s);
 }
 
 extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, void* out,

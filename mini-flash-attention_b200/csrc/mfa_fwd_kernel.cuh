@@ -43,7 +43,7 @@
 
 namespace mfa {
 
-template <int NQ_, int STAGES_, bool CAUSAL_, bool BF16_>
+template <int NQ_, int STAGES_, bool CAUSAL_, bool BF16_, int D_>
 struct FwdConfig {
   static constexpr int NQ = NQ_;
   static constexpr int STAGES = STAGES_;
@@ -52,8 +52,16 @@ struct FwdConfig {
   static constexpr int kRows = 128;       // query rows per tile (= MMA M)
   static constexpr int kRowsPerUnit = kRows * NQ;
   static constexpr int kKeys = 128;       // keys per block (= S tile N)
-  static constexpr int kHeadDim = 64;
-  static constexpr int kTileBytes = kRows * kHeadDim * 2;  // 16 KiB, one TMA box
+  static constexpr int kHeadDim = D_;     // 32, 64 or 128
+  static constexpr int kTileBytes = kRows * kHeadDim * 2;  // one 128-row tile of q, k or v
+  // A tile arrives as D / 64 TMA boxes of 64 columns (128-byte rows, 128-byte swizzle), or
+  // for D = 32 as one box of 32 columns (64-byte rows, 64-byte swizzle); boxes are stored
+  // one after the other. The MMA operand descriptors follow the same atoms.
+  static constexpr int kBoxCols = kHeadDim < 64 ? kHeadDim : 64;
+  static constexpr int kBoxes = kHeadDim / kBoxCols;
+  static constexpr int kRowBytes = kBoxCols * 2;          // bytes of one box row = swizzle span
+  static constexpr int kBoxBytes = kRows * kRowBytes;
+  static constexpr int kSwizzleChunks = kRowBytes / 16;   // 16-byte chunks per swizzled row
   static constexpr int kSoftmaxWarps = 8 * NQ;   // two warps per TMEM lane quadrant and tile
   static constexpr int kMmaWarp = kSoftmaxWarps;
   static constexpr int kLoadWarp = kSoftmaxWarps + 1;
@@ -67,7 +75,7 @@ struct FwdConfig {
   static constexpr int kSoftmaxRegs = 104;
   static constexpr int kControlRegs = 64;
 
-  // shared memory (offsets from a 1024-aligned base; 128B swizzle atoms need 1024 alignment)
+  // shared memory (offsets from a 1024-aligned base; swizzle atoms need 1024 / 512 alignment)
   static constexpr int kQOff = 0;                              // two Q buffers of NQ tiles
   static constexpr int kKOff = kQOff + 2 * NQ * kTileBytes;
   static constexpr int kVOff = kKOff + STAGES * kTileBytes;
@@ -91,13 +99,14 @@ struct FwdConfig {
   static constexpr int kSmemUsed = kAbortOff + 4;
   static constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for manual 1024 alignment
 
-  // tensor memory columns
-  static constexpr int kTmemCols = NQ == 2 ? 512 : 256;
+  // tensor memory columns: S_i (128 fp32), P_i (64 fp16 pairs), O_i (D fp32)
   static constexpr int kColS = 0;
   static constexpr int kColP = 128 * NQ;
   static constexpr int kColO = 192 * NQ;
+  static constexpr int kTmemUsed = kColO + kHeadDim * NQ;
+  static constexpr int kTmemCols = kTmemUsed <= 256 ? 256 : 512;  // allocation: a power of 2
 
-  // one partial-result slot: O[rows][64] fp32 (unnormalised), then m[rows], l[rows]
+  // one partial-result slot: O[rows][D] fp32 (unnormalised), then m[rows], l[rows]
   static constexpr int kSlotFloats = kRowsPerUnit * (kHeadDim + 2);
 
   static constexpr float kRescaleThreshold = 8.0f;
@@ -110,7 +119,8 @@ struct FwdConfig {
                     4 * 32 * kSoftmaxRegs * 4 + 4 * 32 * kControlRegs == kThreads * kLaunchRegs,
                 "register split must use exactly the launch allocation");
   static_assert(!kRebalanceRegs || 4 * kSoftmaxRegs + kControlRegs <= 512, "per sub-partition");
-  static_assert(kColO + 64 * NQ <= kTmemCols, "TMEM budget");
+  static_assert(kTmemUsed <= 512, "TMEM budget");
+  static_assert(kHeadDim == 32 || kHeadDim == 64 || kHeadDim == 128, "head dim");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -224,9 +234,12 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
       mbar_arrive_expect_tx(bar(Cfg::kBarQFull + b), Cfg::NQ * Cfg::kTileBytes);
 #pragma unroll
       for (int i = 0; i < Cfg::NQ; ++i) {
-        tma_load_4d(sbase + Cfg::kQOff + (b * Cfg::NQ + i) * Cfg::kTileBytes, &p.tm_q,
-                    bar(Cfg::kBarQFull + b), 0,
-                    (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, hb.h, hb.b);
+#pragma unroll
+        for (int x = 0; x < Cfg::kBoxes; ++x) {
+          tma_load_4d(sbase + Cfg::kQOff + (b * Cfg::NQ + i) * Cfg::kTileBytes + x * Cfg::kBoxBytes,
+                      &p.tm_q, bar(Cfg::kBarQFull + b), x * Cfg::kBoxCols,
+                      (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, hb.h, hb.b);
+        }
       }
       q_loaded = s + 1;
     }
@@ -234,13 +247,21 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
     const uint32_t ph = static_cast<uint32_t>(g / ST) & 1u;
     if (!wait_single(bar(Cfg::kBarKEmpty + st), ph ^ 1u, wd, kSiteLoadKEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarKFull + st), Cfg::kTileBytes);
-    tma_load_4d_hint(sbase + Cfg::kKOff + st * Cfg::kTileBytes, &p.tm_k, bar(Cfg::kBarKFull + st),
-                     0, cur.j * Cfg::kKeys, hb.h, hb.b, keep);
+#pragma unroll
+    for (int x = 0; x < Cfg::kBoxes; ++x) {
+      tma_load_4d_hint(sbase + Cfg::kKOff + st * Cfg::kTileBytes + x * Cfg::kBoxBytes, &p.tm_k,
+                       bar(Cfg::kBarKFull + st), x * Cfg::kBoxCols, cur.j * Cfg::kKeys, hb.h,
+                       hb.b, keep);
+    }
     k_issued = g + 1;
     if (!wait_single(bar(Cfg::kBarVEmpty + st), ph ^ 1u, wd, kSiteLoadVEmpty)) break;
     mbar_arrive_expect_tx(bar(Cfg::kBarVFull + st), Cfg::kTileBytes);
-    tma_load_4d_hint(sbase + Cfg::kVOff + st * Cfg::kTileBytes, &p.tm_v, bar(Cfg::kBarVFull + st),
-                     0, cur.j * Cfg::kKeys, hb.h, hb.b, keep);
+#pragma unroll
+    for (int x = 0; x < Cfg::kBoxes; ++x) {
+      tma_load_4d_hint(sbase + Cfg::kVOff + st * Cfg::kTileBytes + x * Cfg::kBoxBytes, &p.tm_v,
+                       bar(Cfg::kBarVFull + st), x * Cfg::kBoxCols, cur.j * Cfg::kKeys, hb.h,
+                       hb.b, keep);
+    }
     v_issued = g + 1;
     ++g;
     cur.step(p);
@@ -275,15 +296,24 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
   const uint32_t sbase = smem_addr(smem);
   constexpr uint32_t kIdescS = idesc_f16_f32(128, 128, false, Cfg::kBF16);
-  constexpr uint32_t kIdescO = idesc_f16_f32(128, 64, true, Cfg::kBF16);
-  // K-major Q / K tiles: SBO = 1024 (8-row swizzle atoms), LBO unused (16). MN-major V tile
-  // (d contiguous): SBO = 1024 between 8-key groups, LBO = one tile (unused: the 64
-  // d-columns are a single 128-byte swizzle atom).
-  constexpr uint32_t kHi = smem_desc_hi(1024, kSwizzle128B);
+  constexpr uint32_t kIdescO = idesc_f16_f32(128, Cfg::kHeadDim, true, Cfg::kBF16);
+  // Swizzle atoms are 8 rows of kRowBytes (128 B, or 64 B for D = 32). K-major Q / K tiles:
+  // SBO = one atom (8 rows), LBO unused (16); the K steps of 16 head dims (32 bytes) walk
+  // through an atom and then on to the next box. MN-major V tile (d contiguous): SBO = one
+  // atom between 8-key groups, LBO = one box between the 64-column halves of D = 128 (unused
+  // when D fits one atom).
+  constexpr uint64_t kSwz = Cfg::kRowBytes == 128 ? kSwizzle128B : kSwizzle64B;
+  constexpr uint32_t kHi = smem_desc_hi(8 * Cfg::kRowBytes, kSwz);
   const uint32_t q_lo = smem_desc_lo(sbase + Cfg::kQOff, 16);
   const uint32_t k_lo = smem_desc_lo(sbase + Cfg::kKOff, 16);
-  const uint32_t v_lo = smem_desc_lo(sbase + Cfg::kVOff, Cfg::kTileBytes);
+  const uint32_t v_lo = smem_desc_lo(sbase + Cfg::kVOff, Cfg::kBoxBytes);
   constexpr uint32_t kTileStep = Cfg::kTileBytes >> 4;
+  constexpr int kStepsPerBox = Cfg::kBoxCols / 16;
+  // descriptor offset (16-byte units) of K step kk of a K-major tile
+  auto k_off = [](int kk) -> uint32_t {
+    return static_cast<uint32_t>((kk / kStepsPerBox) * (Cfg::kBoxBytes >> 4) +
+                                 (kk % kStepsPerBox) * 2);
+  };
   const bool leader = elect_one();
   bool issued_any = false;
 
@@ -315,9 +345,9 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
         const uint32_t qd = q_lo + (b * NQ + i) * kTileStep;
         const uint32_t d_tmem = tmem + Cfg::kColS + 128 * i;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {  // 16 of the 64 head dims per MMA (32 bytes)
-          mma_ss(d_tmem, desc_join(qd + 2 * kk, kHi), desc_join(kd + 2 * kk, kHi), kIdescS,
-                 kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < Cfg::kHeadDim / 16; ++kk) {  // 16 head dims per MMA (32 bytes)
+          mma_ss(d_tmem, desc_join(qd + k_off(kk), kHi), desc_join(kd + k_off(kk), kHi),
+                 kIdescS, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar(Cfg::kBarSFull + i));
       }
@@ -350,11 +380,11 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
           goto unwind;
         tc_fence_after();
         if (leader) {
-          const uint32_t d_tmem = tmem + Cfg::kColO + 64 * i;
+          const uint32_t d_tmem = tmem + Cfg::kColO + Cfg::kHeadDim * i;
           const uint32_t a_tmem = tmem + Cfg::kColP + 64 * i;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: two 8-key swizzle atoms (2 KiB)
-            mma_ts(d_tmem, a_tmem + 8 * kk, desc_join(vd + 128 * kk, kHi), kIdescO,
+          for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: two 8-key swizzle atoms
+            mma_ts(d_tmem, a_tmem + 8 * kk, desc_join(vd + Cfg::kRowBytes * kk, kHi), kIdescO,
                    (!fresh || kk > 0) ? 1u : 0u);
           }
           mma_commit(bar(Cfg::kBarODone + i));
@@ -397,7 +427,7 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
     return false;
   tc_fence_after();
   uint32_t sr[64];  // sr[4i + e]: row g + 8 (e / 2), key 8i + 2q + e % 2
-  tmem_ld_16x256b_x16_sync(tS, sr);
+  tmem_ld_16x256b_sync(tS, sr);
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(bar(Cfg::kBarSFree + tile));
@@ -508,11 +538,12 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
   }
   tmem_st_16x128b_x16(tP, pk);
   if (grow && !first) {
-    uint32_t o[32];  // o[4i + e]: row g + 8 (e / 2), d 8i + 2q + e % 2
-    tmem_ld_16x256b_x8_sync(tO, o);
+    uint32_t o[Cfg::kHeadDim / 2];  // o[4i + e]: row g + 8 (e / 2), d 8i + 2q + e % 2
+    tmem_ld_16x256b_sync(tO, o);
 #pragma unroll
-    for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(f(o[k]) * alpha[(k >> 1) & 1]);
-    tmem_st_16x256b_x8(tO, o);
+    for (int k = 0; k < Cfg::kHeadDim / 2; ++k)
+      o[k] = __float_as_uint(f(o[k]) * alpha[(k >> 1) & 1]);
+    tmem_st_16x256b(tO, o);
   }
   tmem_wait_st();
   tc_fence_before();
@@ -535,7 +566,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   const uint32_t lane_bits = static_cast<uint32_t>(slice) << 16;
   const uint32_t tS = tmem + lane_bits + Cfg::kColS + 128 * tile;
   const uint32_t tP = tmem + lane_bits + Cfg::kColP + 64 * tile;
-  const uint32_t tO = tmem + lane_bits + Cfg::kColO + 64 * tile;
+  const uint32_t tO = tmem + lane_bits + Cfg::kColO + Cfg::kHeadDim * tile;
   const bool tile_leader = (warp & 7) == 0 && lane == 0;
 
   int g = 0;       // global step index (phase of the per-step barriers)
@@ -563,8 +594,8 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
       l_row[r] = l_run[r] + __shfl_xor_sync(0xffffffffu, l_run[r], 1);
       l_row[r] += __shfl_xor_sync(0xffffffffu, l_row[r], 2);
     }
-    uint32_t o[32];  // o[4i + e]: row gq + 8 (e / 2), d 8i + 2q + e % 2
-    tmem_ld_16x256b_x8_sync(tO, o);
+    uint32_t o[Cfg::kHeadDim / 2];  // o[4i + e]: row gq + 8 (e / 2), d 8i + 2q + e % 2
+    tmem_ld_16x256b_sync(tO, o);
     tc_fence_before();
     const int b = cur.seg_idx & 1;
     if (cur.whole(p.sc)) {
@@ -574,11 +605,16 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
       for (int r = 0; r < 2; ++r) {
         const int row = slice + gq + 8 * r;
         const float inv_l = 1.0f / l_row[r];
+        // the TMA box layout: box x holds columns [64x, 64x + 64); in a row of kRowBytes
+        // the 16-byte chunk c sits at c ^ (row-address bits 7.., the swizzle pattern)
+        const int swz = ((row * Cfg::kRowBytes) >> 7) & (Cfg::kSwizzleChunks - 1);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {  // 16-byte chunk i of the row, 4 bytes per thread
+        for (int i = 0; i < Cfg::kHeadDim / 8; ++i) {  // 16-byte chunk i, 4 bytes per thread
           const uint32_t w = pack_pair<Cfg::kBF16>(__uint_as_float(o[4 * i + 2 * r]) * inv_l,
                                                    __uint_as_float(o[4 * i + 2 * r + 1]) * inv_l);
-          const uint32_t dst = smem_addr(stage + row * 128 + ((i ^ (row & 7)) << 4) + 4 * q);
+          const int x = i / Cfg::kSwizzleChunks, c = i % Cfg::kSwizzleChunks;
+          const uint32_t dst = smem_addr(stage + x * Cfg::kBoxBytes + row * Cfg::kRowBytes +
+                                         ((c ^ swz) << 4) + 4 * q);
           asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst), "r"(w) : "memory");
         }
       }
@@ -594,7 +630,10 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
         const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
         if (r0 < p.n) {
           const HeadBatch ob = head_batch(p, cur.u);
-          tma_store_4d(&p.tm_o, smem_addr(stage), 0, r0, ob.h, ob.b);
+#pragma unroll
+          for (int x = 0; x < Cfg::kBoxes; ++x)
+            tma_store_4d(&p.tm_o, smem_addr(stage + x * Cfg::kBoxBytes), x * Cfg::kBoxCols, r0,
+                         ob.h, ob.b);
           tma_store_commit();
           tma_store_wait_read();
         }
@@ -612,7 +651,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
         const int row = tile * Cfg::kRows + slice + gq + 8 * r;
         float2* dst = reinterpret_cast<float2*>(ws + static_cast<size_t>(row) * Cfg::kHeadDim);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < Cfg::kHeadDim / 8; ++i)
           dst[4 * i + q] = make_float2(__uint_as_float(o[4 * i + 2 * r]),
                                        __uint_as_float(o[4 * i + 2 * r + 1]));
         if (q == 0) {
@@ -627,10 +666,10 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   }
 }
 
-template <int NQ, int STAGES, bool CAUSAL, bool BF16>
-__global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16>::kThreads, 1)
+template <int NQ, int STAGES, bool CAUSAL, bool BF16, int D>
+__global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D>::kThreads, 1)
     mfa_fwd_kernel(const __grid_constant__ FwdParams p) {
-  using Cfg = FwdConfig<NQ, STAGES, CAUSAL, BF16>;
+  using Cfg = FwdConfig<NQ, STAGES, CAUSAL, BF16, D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -714,10 +753,9 @@ struct MergeParams {
 // grid has completed and its writes are visible.
 constexpr int kMergeThreadsPerRow = 4;
 
-template <int kRowsPerUnit, int kSlotFloats, bool kCausal, bool kBF16>
+template <int kRowsPerUnit, int kSlotFloats, bool kCausal, bool kBF16, int kD>
 __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
     mfa_merge_kernel(const MergeParams mp) {
-  constexpr int kD = 64;
   constexpr int kChunks = kD / 4 / kMergeThreadsPerRow;  // float4 chunks per thread
   const int c = static_cast<int>(blockIdx.x);
   const long long total = mp.sc.total();

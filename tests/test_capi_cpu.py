@@ -143,8 +143,9 @@ def test_general_entry_validates_dtype_layout_and_shape():
         return e.value
     assert call(dtype=7).code == capi.MFA_ERR_INVALID_ARGUMENT
     assert call(layout=5).code == capi.MFA_ERR_INVALID_ARGUMENT
-    e = call(d=128)
-    assert (e.code, str(e)) == (capi.MFA_ERR_HEAD_DIM, "This kernel supports only D=64")
+    e = call(d=96)
+    assert (e.code, str(e)) == (capi.MFA_ERR_HEAD_DIM,
+                                "This kernel supports only D=32, D=64 and D=128")
     assert call(n=200).code in (capi.MFA_ERR_CUDA, capi.MFA_ERR_DEVICE)
     assert call(batch=-1).code == capi.MFA_ERR_INVALID_ARGUMENT
     # valid arguments reach the device (no GPU here)

@@ -174,9 +174,12 @@ def test_errors_match_reference_messages():
         mfa.forward(q.reshape(128, 64), q.reshape(128, 64), q.reshape(128, 64))
     with pytest.raises(RuntimeError, match="k must have the same shape as q"):
         mfa.forward(q, q[:, :, :64].contiguous(), q)
-    with pytest.raises(RuntimeError, match="This kernel supports only D=64"):
-        x = torch.zeros(1, 1, 128, 32, device="cuda", dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="This kernel supports only D=32, D=64 and D=128"):
+        x = torch.zeros(1, 1, 128, 48, device="cuda", dtype=torch.float16)
         mfa.forward(x, x, x)
+    with pytest.raises(RuntimeError, match="This WMMA prototype supports only D=64 yet"):
+        x = torch.zeros(1, 1, 128, 32, device="cuda", dtype=torch.float16)
+        mfa.forward_wmma(x, x, x)
     with pytest.raises(RuntimeError, match="Only N \\(seq len\\) divisible by 64 and 64"):
         x = torch.zeros(1, 1, 96, 64, device="cuda", dtype=torch.float16)
         mfa.forward_wmma(x, x, x)
