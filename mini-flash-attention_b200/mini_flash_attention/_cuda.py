@@ -34,8 +34,8 @@ def _load_extension():
 
 
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False) -> torch.Tensor:
-    """softmax(q k^T / sqrt(D)) v on [B, H, N, D] (or [B*H, N, D]) tensors, fp16 or bf16;
-    causal=True masks key index > query index."""
+    """softmax(q k^T / sqrt(D)) v on [B, H, N, D] (or [B*H, N, D]) tensors: fp16 or bf16,
+    D = 32, 64 or 128, any N; causal=True masks key index > query index."""
     return _load_extension().forward(q, k, v, causal)
 
 
