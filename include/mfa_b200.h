@@ -82,6 +82,30 @@ MFA_API int mfa_fwd(const void* q, const void* k, const void* v, void* out, int6
                     int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
                     int32_t dtype, int32_t layout, void* stream);
 
+/*
+ * mfa_fwd that also writes the row log-sum-exp of the scaled scores,
+ * lse[bh * N + row] = ln(sum over keys of exp(scale * q.k)), fp32 [B*H, N] whatever the
+ * layout: the state the backward pass needs. No counterpart in the reference (no backward).
+ */
+MFA_API int mfa_fwd_lse(const void* q, const void* k, const void* v, void* out, float* lse,
+                        int64_t batch, int64_t heads, int64_t n, int32_t d, float scale,
+                        int32_t causal, int32_t dtype, int32_t layout, void* stream);
+
+/*
+ * Backward pass (D = 64, fp16 or bf16, either layout, any N, optional causal mask): from q,
+ * k, v, the forward output `out`, its gradient `dout` and `lse` of mfa_fwd_lse (same scale and
+ * causal), writes dq, dk, dv (type and layout of q). dV = P^T dout, dS = P * (dout v^T - D)
+ * with D = rowsum(dout * out), dq = scale * dS k, dk = scale * dS^T q. Two tcgen05 passes
+ * (dq; dk and dv) and a small row pass; a stream-ordered scratch of 8 bytes per row from the
+ * library's pool. Other D: MFA_ERR_HEAD_DIM "The backward pass supports only D=64". No
+ * counterpart in the reference: its README lists the backward pass as future work
+ * (README.md:125).
+ */
+MFA_API int mfa_bwd(const void* q, const void* k, const void* v, const void* out,
+                    const void* dout, const float* lse, void* dq, void* dk, void* dv,
+                    int64_t batch, int64_t heads, int64_t n, int32_t d, float scale,
+                    int32_t causal, int32_t dtype, int32_t layout, void* stream);
+
 /* Size of the static device scratch array used by mfa_fwd_f16_noalloc (20 MiB). */
 #define MFA_NOALLOC_SCRATCH_BYTES 20971520u
 

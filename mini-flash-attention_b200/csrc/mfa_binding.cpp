@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <limits>
 #include <stdexcept>
+#include <vector>
 
 #include "mfa_b200.h"
 
@@ -120,6 +121,59 @@ torch::Tensor flash_attn_forward_wmma(torch::Tensor q, torch::Tensor k, torch::T
   return out;
 }
 
+// forward plus the row log-sum-exp (fp32 [B*H, N] viewed as q's leading dims + N).
+std::vector<torch::Tensor> flash_attn_forward_lse(torch::Tensor q, torch::Tensor k,
+                                                  torch::Tensor v, bool causal) {
+  check_forward_inputs(q, k, v, true, Layout::kBHND);
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  auto out = torch::empty_like(q);
+  auto lse_shape = q.sizes().vec();
+  lse_shape.pop_back();
+  auto lse = torch::empty(lse_shape, q.options().dtype(torch::kFloat32));
+  const Extents e = extents_of(q, Layout::kBHND);
+  const float scale = 1.0f / std::sqrt(static_cast<float>(e.d));
+  const int dtype = q.scalar_type() == torch::kBFloat16 ? MFA_DTYPE_BF16 : MFA_DTYPE_FP16;
+  const int rc = mfa_fwd_lse(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                             lse.data_ptr<float>(), e.batch, e.heads, e.n,
+                             static_cast<int32_t>(e.d), scale, causal ? 1 : 0, dtype,
+                             MFA_LAYOUT_BHND,
+                             static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
+  if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
+  return {out, lse};
+}
+
+// Backward of forward: dq, dk, dv from q, k, v, out, lse (of forward_lse) and dout.
+std::vector<torch::Tensor> flash_attn_backward(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                               torch::Tensor out, torch::Tensor lse,
+                                               torch::Tensor dout, bool causal) {
+  check_forward_inputs(q, k, v, true, Layout::kBHND);
+  TORCH_CHECK(out.is_cuda() && out.device() == q.device() && dout.is_cuda() &&
+                  dout.device() == q.device() && lse.is_cuda() && lse.device() == q.device(),
+              "out, lse and dout must be on q's device");
+  TORCH_CHECK(out.sizes() == q.sizes() && dout.sizes() == q.sizes(),
+              "out and dout must have the same shape as q");
+  TORCH_CHECK(out.scalar_type() == q.scalar_type() && dout.scalar_type() == q.scalar_type(),
+              "out and dout must have q's dtype");
+  TORCH_CHECK(out.is_contiguous() && dout.is_contiguous() && lse.is_contiguous(),
+              "out, lse and dout must be contiguous");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32, "lse must be float32");
+  TORCH_CHECK(lse.numel() * q.size(-1) == q.numel(), "lse must have one value per query row");
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  auto dq = torch::empty_like(q);
+  auto dk = torch::empty_like(k);
+  auto dv = torch::empty_like(v);
+  const Extents e = extents_of(q, Layout::kBHND);
+  const float scale = 1.0f / std::sqrt(static_cast<float>(e.d));
+  const int dtype = q.scalar_type() == torch::kBFloat16 ? MFA_DTYPE_BF16 : MFA_DTYPE_FP16;
+  const int rc = mfa_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                         dout.data_ptr(), lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(),
+                         dv.data_ptr(), e.batch, e.heads, e.n, static_cast<int32_t>(e.d), scale,
+                         causal ? 1 : 0, dtype, MFA_LAYOUT_BHND,
+                         static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
+  if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
+  return {dq, dk, dv};
+}
+
 // Same as forward, writing into a caller-provided contiguous tensor of q's shape and dtype
 // (used by the pipelined host-buffer path to fill slices of one device buffer).
 void flash_attn_forward_into(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
@@ -137,6 +191,10 @@ void flash_attn_forward_into(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward", &flash_attn_forward, "Mini Flash Attention forward (sm_100a tcgen05)");
+  m.def("forward_lse", &flash_attn_forward_lse,
+        "Mini Flash Attention forward returning (out, lse), lse = row log-sum-exp (fp32)");
+  m.def("backward", &flash_attn_backward,
+        "Mini Flash Attention backward: (dq, dk, dv) from q, k, v, out, lse, dout (D = 64)");
   m.def("forward_bnhd", &flash_attn_forward_bnhd,
         "Mini Flash Attention forward on [B, N, H, D] tensors (fp16 or bf16)");
   m.def("forward_wmma", &flash_attn_forward_wmma,

@@ -16,6 +16,7 @@
 #include <string>
 
 #include "../../include/mfa_b200.h"
+#include "mfa_bwd_kernel.cuh"
 #include "mfa_fwd_kernel.cuh"
 
 namespace mfa {
@@ -43,6 +44,25 @@ cudaError_t set_smem_attribute() {
   return cudaFuncSetAttribute(
       mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim>,
       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+}
+
+template <bool kDKV, bool kCausal, bool kBF16>
+cudaError_t set_bwd_attribute() {
+  return cudaFuncSetAttribute(mfa_bwd_kernel<kDKV, kCausal, kBF16>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              BwdConfig<kDKV, kCausal, kBF16>::kSmemBytes);
+}
+
+cudaError_t set_bwd_attributes() {
+  cudaError_t e = set_bwd_attribute<false, false, false>();
+  if (e == cudaSuccess) e = set_bwd_attribute<false, true, false>();
+  if (e == cudaSuccess) e = set_bwd_attribute<false, false, true>();
+  if (e == cudaSuccess) e = set_bwd_attribute<false, true, true>();
+  if (e == cudaSuccess) e = set_bwd_attribute<true, false, false>();
+  if (e == cudaSuccess) e = set_bwd_attribute<true, true, false>();
+  if (e == cudaSuccess) e = set_bwd_attribute<true, false, true>();
+  if (e == cudaSuccess) e = set_bwd_attribute<true, true, true>();
+  return e;
 }
 
 template <int D>
@@ -117,6 +137,7 @@ int prepare_device(int dev) {
     if (e == cudaSuccess) e = set_smem_attributes_d<32>();
     if (e == cudaSuccess) e = set_smem_attributes_d<64>();
     if (e == cudaSuccess) e = set_smem_attributes_d<128>();
+    if (e == cudaSuccess) e = set_bwd_attributes();
     if (e == cudaSuccess) e = set_smem_attribute<Simple<false>>();
     if (e == cudaSuccess) e = set_smem_attribute<Simple<true>>();
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ds.status_ptr), g_device_status);
@@ -246,7 +267,8 @@ int plan_forward(int64_t bh, int64_t n, int64_t sms, Plan& pl) {
 template <class Cfg>
 cudaError_t launch_planned(const void* q, const void* k, const void* v, void* out, int64_t batch,
                            int64_t heads, int64_t n, int layout, float scale, const Plan& pl,
-                           float* workspace, int* status_ptr, cudaStream_t stream, int* rc) {
+                           float* workspace, int* status_ptr, cudaStream_t stream, int* rc,
+                           float* lse = nullptr) {
   FwdParams p;
   *rc = MFA_OK;
   const bool bf16 = Cfg::kBF16;
@@ -267,6 +289,7 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
   p.timeout_ns = g_watchdog_ns;
   p.status = status_ptr;
   p.workspace = workspace;
+  p.lse = lse;
   mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim>
       <<<static_cast<unsigned>(pl.ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
@@ -274,6 +297,7 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
     const Strides st = layout_strides(layout, heads, n, d);
     MergeParams mp;
     mp.out = out;
+    mp.lse = lse;
     mp.workspace = workspace;
     mp.n = p.n;
     mp.heads = p.heads;
@@ -291,7 +315,8 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
 // pool, freed on the same stream.
 template <class Cfg>
 int launch_forward(const void* q, const void* k, const void* v, void* out, int64_t batch,
-                   int64_t heads, int64_t n, int layout, float scale, cudaStream_t stream) {
+                   int64_t heads, int64_t n, int layout, float scale, cudaStream_t stream,
+                   float* lse = nullptr) {
   const int64_t bh = batch * heads;
   if (bh == 0 || n == 0) return MFA_OK;
   int dev = 0;
@@ -309,7 +334,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
     if (e != cudaSuccess) return fail_cuda(e, "cudaMallocFromPoolAsync (split workspace)");
   }
   e = launch_planned<Cfg>(q, k, v, out, batch, heads, n, layout, scale, pl, workspace,
-                          g_devices[dev].status_ptr, stream, &rc);
+                          g_devices[dev].status_ptr, stream, &rc, lse);
   if (pl.split) {
     const cudaError_t ef = cudaFreeAsync(workspace, stream);
     if (e == cudaSuccess) e = ef;
@@ -508,23 +533,21 @@ namespace {
 template <int D>
 int launch_general(const void* q, const void* k, const void* v, void* out, int64_t batch,
                    int64_t heads, int64_t n, float scale, int32_t causal, int32_t dtype,
-                   int32_t layout, cudaStream_t s) {
+                   int32_t layout, cudaStream_t s, float* lse) {
   if (dtype == MFA_DTYPE_BF16)
     return causal ? launch_forward<Full<true, true, D>>(q, k, v, out, batch, heads, n, layout,
-                                                        scale, s)
+                                                        scale, s, lse)
                   : launch_forward<Full<false, true, D>>(q, k, v, out, batch, heads, n, layout,
-                                                         scale, s);
+                                                         scale, s, lse);
   return causal ? launch_forward<Full<true, false, D>>(q, k, v, out, batch, heads, n, layout,
-                                                       scale, s)
+                                                       scale, s, lse)
                 : launch_forward<Full<false, false, D>>(q, k, v, out, batch, heads, n, layout,
-                                                        scale, s);
+                                                        scale, s, lse);
 }
-}  // namespace
-}  // namespace mfa
 
-extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, int64_t batch,
-                       int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
-                       int32_t dtype, int32_t layout, void* stream) {
+int fwd_general(const void* q, const void* k, const void* v, void* out, float* lse,
+                int64_t batch, int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
+                int32_t dtype, int32_t layout, void* stream) {
   if (batch < 0 || heads < 0) return fail(MFA_ERR_INVALID_ARGUMENT, "negative extent");
   if (heads > 0 && batch > 0x7fffffffLL / heads)
     return fail(MFA_ERR_INVALID_ARGUMENT, "B * H is too large");
@@ -537,11 +560,148 @@ extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, i
   if (layout != MFA_LAYOUT_BHND && layout != MFA_LAYOUT_BNHD)
     return fail(MFA_ERR_INVALID_ARGUMENT, "layout must be MFA_LAYOUT_BHND or MFA_LAYOUT_BNHD");
   if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  if (batch * heads > 0 && n > 0 && lse != nullptr) {
+    if (reinterpret_cast<uintptr_t>(lse) & 3u)
+      return fail(MFA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (d == 32) return launch_general<32>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s);
+  if (d == 32)
+    return launch_general<32>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s, lse);
   if (d == 128)
-    return launch_general<128>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s);
-  return launch_general<64>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s);
+    return launch_general<128>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s,
+                               lse);
+  return launch_general<64>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s, lse);
+}
+
+// ---------------------------------------------------------------- backward
+template <bool kDKV, bool kCausal, bool kBF16>
+cudaError_t launch_bwd_pass(BwdParams& bp, const void* x, const void* y, const void* s0,
+                            const void* s1, void* o0, void* o1, int64_t batch, int64_t heads,
+                            int64_t n, int layout, int64_t ctas, cudaStream_t stream, int* rc) {
+  *rc = MFA_OK;
+  if ((*rc = encode_tensor(&bp.tm_x, x, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (*rc = encode_tensor(&bp.tm_y, y, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (*rc = encode_tensor(&bp.tm_s0, s0, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (*rc = encode_tensor(&bp.tm_s1, s1, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (*rc = encode_tensor(&bp.tm_o0, o0, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (*rc = encode_tensor(&bp.tm_o1, o1 ? o1 : o0, batch, heads, n, 64, layout, kBF16)) != MFA_OK)
+    return cudaSuccess;
+  using Cfg = BwdConfig<kDKV, kCausal, kBF16>;
+  mfa_bwd_kernel<kDKV, kCausal, kBF16>
+      <<<static_cast<unsigned>(ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(bp);
+  return cudaGetLastError();
+}
+
+template <bool kCausal, bool kBF16>
+int launch_backward(const void* q, const void* k, const void* v, const void* out,
+                    const void* dout, const float* lse, void* dq, void* dk, void* dv,
+                    int64_t batch, int64_t heads, int64_t n, int layout, float scale,
+                    cudaStream_t stream) {
+  const int64_t bh = batch * heads;
+  if (bh == 0 || n == 0) return MFA_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  int rc = prepare_device(dev);
+  if (rc != MFA_OK) return rc;
+  if ((rc = check_device_pointers(q, k, v, out, dev)) != MFA_OK) return rc;
+  if ((rc = check_device_pointers(dout, dq, dk, dv, dev)) != MFA_OK) return rc;
+  if ((rc = check_device_pointers(lse, lse, lse, lse, dev)) != MFA_OK) return rc;
+  const int64_t blocks = (n + 127) / 128;
+  const int64_t units = bh * blocks;
+  if (units > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  const int64_t sms = g_devices[dev].num_sms;
+  const int64_t ctas = units < sms ? units : sms;
+  // L2 and D per row, padded to whole 128-row blocks per head
+  const size_t rows = static_cast<size_t>(units) * 128;
+  float* ws = nullptr;
+  e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), 2 * rows * sizeof(float),
+                              g_devices[dev].pool, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMallocFromPoolAsync (backward workspace)");
+  float* lse2 = ws;
+  float* di = ws + rows;
+  const Strides st = layout_strides(layout, heads, n, 64);
+  const int64_t prep_blocks_needed = (static_cast<int64_t>(rows) / 4 + 7) / 8;
+  const unsigned prep_grid =
+      static_cast<unsigned>(prep_blocks_needed < sms * 16 ? prep_blocks_needed : sms * 16);
+  mfa_bwd_prep_kernel<kBF16><<<prep_grid, 256, 0, stream>>>(
+      out, dout, lse, lse2, di, static_cast<int>(bh), static_cast<int>(n),
+      static_cast<int>(heads), st.b, st.h, st.n, static_cast<int>(blocks));
+  e = cudaGetLastError();
+  BwdParams bp;
+  bp.n = static_cast<int>(n);
+  bp.heads = static_cast<int>(heads);
+  bp.bh = static_cast<int>(bh);
+  bp.blocks = static_cast<int>(blocks);
+  bp.scale = scale;
+  bp.scale_log2 = scale * 1.4426950408889634f;
+  bp.lse2 = lse2;
+  bp.di = di;
+  bp.timeout_ns = g_watchdog_ns;
+  bp.status = g_devices[dev].status_ptr;
+  if (e == cudaSuccess && rc == MFA_OK)  // dQ: q, dO resident; k, v streamed
+    e = launch_bwd_pass<false, kCausal, kBF16>(bp, q, dout, k, v, dq, nullptr, batch, heads, n,
+                                               layout, ctas, stream, &rc);
+  if (e == cudaSuccess && rc == MFA_OK)  // dK, dV: k, v resident; q, dO streamed
+    e = launch_bwd_pass<true, kCausal, kBF16>(bp, k, v, q, dout, dk, dv, batch, heads, n,
+                                              layout, ctas, stream, &rc);
+  const cudaError_t ef = cudaFreeAsync(ws, stream);
+  if (rc != MFA_OK) return rc;
+  if (e == cudaSuccess) e = ef;
+  if (e != cudaSuccess) return fail_cuda(e, "backward launch");
+  return MFA_OK;
+}
+
+}  // namespace
+}  // namespace mfa
+
+extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                       int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
+                       int32_t dtype, int32_t layout, void* stream) {
+  return fwd_general(q, k, v, out, nullptr, batch, heads, n, d, scale, causal, dtype, layout,
+                     stream);
+}
+
+extern "C" int mfa_fwd_lse(const void* q, const void* k, const void* v, void* out, float* lse,
+                           int64_t batch, int64_t heads, int64_t n, int32_t d, float scale,
+                           int32_t causal, int32_t dtype, int32_t layout, void* stream) {
+  if (!lse && batch * heads > 0 && n > 0)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "null lse pointer");
+  return fwd_general(q, k, v, out, lse, batch, heads, n, d, scale, causal, dtype, layout,
+                     stream);
+}
+
+extern "C" int mfa_bwd(const void* q, const void* k, const void* v, const void* out,
+                       const void* dout, const float* lse, void* dq, void* dk, void* dv,
+                       int64_t batch, int64_t heads, int64_t n, int32_t d, float scale,
+                       int32_t causal, int32_t dtype, int32_t layout, void* stream) {
+  if (batch < 0 || heads < 0) return fail(MFA_ERR_INVALID_ARGUMENT, "negative extent");
+  if (heads > 0 && batch > 0x7fffffffLL / heads)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H is too large");
+  int rc = check_common(q, k, v, const_cast<void*>(out), batch * heads, n, d);
+  if (rc != MFA_OK) return rc;
+  if (batch * heads > 0 && n > 0) {
+    if ((rc = check_common(dout, dq, dk, dv, batch * heads, n, d)) != MFA_OK) return rc;
+    if (!lse) return fail(MFA_ERR_INVALID_ARGUMENT, "null lse pointer");
+    if (reinterpret_cast<uintptr_t>(lse) & 3u)
+      return fail(MFA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
+  }
+  if (d != 64) return fail(MFA_ERR_HEAD_DIM, "The backward pass supports only D=64");
+  if (dtype != MFA_DTYPE_FP16 && dtype != MFA_DTYPE_BF16)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "dtype must be MFA_DTYPE_FP16 or MFA_DTYPE_BF16");
+  if (layout != MFA_LAYOUT_BHND && layout != MFA_LAYOUT_BNHD)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "layout must be MFA_LAYOUT_BHND or MFA_LAYOUT_BNHD");
+  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MFA_DTYPE_BF16)
+    return causal ? launch_backward<true, true>(q, k, v, out, dout, lse, dq, dk, dv, batch,
+                                                heads, n, layout, scale, s)
+                  : launch_backward<false, true>(q, k, v, out, dout, lse, dq, dk, dv, batch,
+                                                 heads, n, layout, scale, s);
+  return causal ? launch_backward<true, false>(q, k, v, out, dout, lse, dq, dk, dv, batch, heads,
+                                               n, layout, scale, s)
+                : launch_backward<false, false>(q, k, v, out, dout, lse, dq, dk, dv, batch,
+                                                heads, n, layout, scale, s);
 }
 
 extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, void* out,

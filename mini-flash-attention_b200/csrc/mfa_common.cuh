@@ -30,6 +30,9 @@ struct FwdParams {
   unsigned long long timeout_ns;  // per-wait watchdog limit
   int* status;                // device status word (0 = ok)
   float* workspace;           // split mode: 2 * gridDim.x partial-result slots
+  // Optional (null: not written): natural-log row log-sum-exp of the scaled scores,
+  // lse[bh * N + row] = ln(sum_k exp(scale * q.k)), for the backward pass.
+  float* lse;
 };
 
 // Status codes written to FwdParams::status by the watchdog: kStatusTimeoutBase + site.
@@ -50,6 +53,11 @@ enum WaitSite : int {
   kSiteLoadQEmpty = 13,
   kSiteSoftXch = 14,
   kSiteSoftStage = 15,
+};
+
+// Head and batch index of a (batch * head) row.
+struct HeadBatch {
+  int h, b;
 };
 
 struct Watchdog {

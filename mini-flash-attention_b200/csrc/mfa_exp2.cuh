@@ -35,7 +35,15 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return r;
 }
 
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 __device__ __forceinline__ uint64_t f2_splat(float x) { return f2_pack(x, x); }
+
+__device__ __forceinline__ uint64_t f2_neg(uint64_t a) { return a ^ 0x8000000080000000ull; }
 
 // 2^x for a pair, on the FMA pipe. Inputs below -125 are clamped (the result is then
 // ~2^-125, i.e. zero for every consumer here); inputs are expected <= 2^22.

@@ -198,9 +198,6 @@ struct StepCursor {
 };
 
 // Head and batch index of unit u: its (batch * head) row is u / q_blocks, heads fastest.
-struct HeadBatch {
-  int h, b;
-};
 __device__ __forceinline__ HeadBatch head_batch(const FwdParams& p, int u) {
   const int bh = u / p.sc.q_blocks;
   return {bh % p.heads, bh / p.heads};
@@ -599,6 +596,17 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     tc_fence_before();
     const int b = cur.seg_idx & 1;
     if (cur.whole(p.sc)) {
+      if (p.lse != nullptr && q == 0) {
+        // log-sum-exp = ln 2 * (m + log2 l), m in scaled log2 units
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int qrow = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows +
+                           slice + gq + 8 * r;
+          if (qrow < p.n)
+            p.lse[static_cast<size_t>(cur.u / p.sc.q_blocks) * p.n + qrow] =
+                (m_run[r] + log2f(l_row[r])) * 0.6931471805599453f;
+        }
+      }
       // O / l -> fp16 -> swizzled staging (this tile's slot of the unit's Q buffer) -> TMA.
       uint8_t* stage = smem + Cfg::kQOff + (b * Cfg::NQ + tile) * Cfg::kTileBytes;
 #pragma unroll
@@ -736,6 +744,7 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D>::kThrea
 // ---------------------------------------------------------------- split-mode merge
 struct MergeParams {
   void* out;          // fp16 / bf16, row (b, h, n) at b * stride_b + h * stride_h + n * stride_n
+  float* lse;         // optional [BH][N] natural-log log-sum-exp (null: not written)
   const float* workspace;
   int n;
   int heads;
@@ -806,6 +815,8 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   const int bh = u / mp.sc.q_blocks;
   const int qrow = (u % mp.sc.q_blocks) * kRowsPerUnit + r;
   if (qrow >= mp.n) return;
+  if (mp.lse != nullptr && k == 0)
+    mp.lse[static_cast<size_t>(bh) * mp.n + qrow] = (m_max + log2f(l)) * 0.6931471805599453f;
   const float inv_l = 1.0f / l;
   const long long offset = static_cast<long long>(bh / mp.heads) * mp.stride_b +
                            static_cast<long long>(bh % mp.heads) * mp.stride_h +

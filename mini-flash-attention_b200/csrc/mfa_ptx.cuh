@@ -133,6 +133,16 @@ __device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int
       : "memory");
 }
 
+// Untiled bulk copy global -> shared, completing `bytes` on the mbarrier (addresses 16-byte
+// aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
@@ -552,6 +562,19 @@ __device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
   return kBF16 ? pack_bf162(lo, hi) : pack_half2(lo, hi);
+}
+
+// Inverse of pack_pair.
+template <bool kBF16>
+__device__ __forceinline__ void unpack_pair(uint32_t w, float& lo, float& hi) {
+  if (kBF16) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xffff0000u);
+  } else {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w);
+    lo = __low2float(h);
+    hi = __high2float(h);
+  }
 }
 
 }  // namespace mfa

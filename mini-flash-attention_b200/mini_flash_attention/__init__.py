@@ -7,9 +7,13 @@ index > query index. ``forward`` takes fp16 or bf16, D = 32, 64 or 128 and any N
 ``forward_wmma`` keeps the reference's contract (fp16, D = 64, N % 64 == 0). There is no CPU or Triton fallback: without the built sm_100a extension
 the calls raise.
 ``forward_bnhd`` is ``forward`` on [B, N, H, D] tensors (the flash-attn layout).
+``forward_lse`` also returns the row log-sum-exp; ``backward`` computes (dq, dk, dv) from it
+(D = 64); ``attention`` is the differentiable forward built from the two.
 ``forward_pinned`` runs the same forward on host tensors, overlapping the host<->device
 copies of batch*head slices with the kernels.
 """
-from ._cuda import forward, forward_bnhd, forward_pinned, forward_wmma
+from ._cuda import (attention, backward, forward, forward_bnhd, forward_lse, forward_pinned,
+                    forward_wmma)
 
-__all__ = ["forward", "forward_wmma", "forward_bnhd", "forward_pinned"]
+__all__ = ["forward", "forward_wmma", "forward_bnhd", "forward_pinned", "forward_lse",
+           "backward", "attention"]

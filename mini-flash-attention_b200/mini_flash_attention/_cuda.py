@@ -39,6 +39,44 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = Fa
     return _load_extension().forward(q, k, v, causal)
 
 
+def forward_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                causal: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """forward plus the row log-sum-exp ln(sum_k exp(q.k / sqrt(D))) as fp32 of shape q.shape[:-1]."""
+    out, lse = _load_extension().forward_lse(q, k, v, causal)
+    return out, lse
+
+
+def backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+             lse: torch.Tensor, dout: torch.Tensor,
+             causal: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients (dq, dk, dv) of forward(q, k, v, causal) for the output gradient dout, given
+    the forward's out and lse (forward_lse). D = 64, fp16 or bf16."""
+    dq, dk, dv = _load_extension().backward(q, k, v, out, lse, dout.contiguous(), causal)
+    return dq, dk, dv
+
+
+class _Attention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal):
+        out, lse = forward_lse(q, k, v, causal)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.causal = causal
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = backward(q, k, v, out, lse, dout, ctx.causal)
+        return dq, dk, dv, None
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+              causal: bool = False) -> torch.Tensor:
+    """Differentiable forward: the tcgen05 forward kernel, with the tcgen05 backward kernels as
+    its autograd backward (D = 64 for gradients)."""
+    return _Attention.apply(q, k, v, causal)
+
+
 def forward_bnhd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                  causal: bool = False) -> torch.Tensor:
     """forward on [B, N, H, D] tensors (the flash-attn layout); the output has that layout."""

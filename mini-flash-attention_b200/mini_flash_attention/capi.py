@@ -16,6 +16,8 @@ EXPORTED_SYMBOLS = (
     "mfa_fwd_simple_f16",
     "mfa_fwd_f16_noalloc",
     "mfa_fwd",
+    "mfa_fwd_lse",
+    "mfa_bwd",
     "mfa_last_error_string",
     "mfa_device_status",
     "mfa_set_watchdog_ns",
@@ -62,6 +64,17 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
                                                     ctypes.c_int32, ctypes.c_int32,
                                                     ctypes.c_void_p]
     lib.mfa_fwd.restype = ctypes.c_int
+    lib.mfa_fwd_lse.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64, ctypes.c_int64,
+                                                        ctypes.c_int64, ctypes.c_int32,
+                                                        ctypes.c_float, ctypes.c_int32,
+                                                        ctypes.c_int32, ctypes.c_int32,
+                                                        ctypes.c_void_p]
+    lib.mfa_fwd_lse.restype = ctypes.c_int
+    lib.mfa_bwd.argtypes = [ctypes.c_void_p] * 9 + [ctypes.c_int64, ctypes.c_int64,
+                                                    ctypes.c_int64, ctypes.c_int32, ctypes.c_float,
+                                                    ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                    ctypes.c_void_p]
+    lib.mfa_bwd.restype = ctypes.c_int
     lib.mfa_last_error_string.argtypes = []
     lib.mfa_last_error_string.restype = ctypes.c_char_p
     lib.mfa_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int]
@@ -109,6 +122,15 @@ def fwd_general(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, he
     """Launch mfa_fwd (dtype and layout selectable); raises MfaError."""
     _check(load().mfa_fwd(q_ptr, k_ptr, v_ptr, out_ptr, batch, heads, n, d, scale, int(causal),
                           dtype, layout, stream))
+
+
+def bwd(q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, do_ptr: int, lse_ptr: int, dq_ptr: int,
+        dk_ptr: int, dv_ptr: int, batch: int, heads: int, n: int, d: int, scale: float,
+        causal: bool = False, dtype: int = DTYPE_FP16, layout: int = LAYOUT_BHND,
+        stream: int = 0) -> None:
+    """Launch mfa_bwd; raises MfaError."""
+    _check(load().mfa_bwd(q_ptr, k_ptr, v_ptr, o_ptr, do_ptr, lse_ptr, dq_ptr, dk_ptr, dv_ptr,
+                          batch, heads, n, d, scale, int(causal), dtype, layout, stream))
 
 
 def device_status(device: int = 0, reset: bool = True) -> int:
