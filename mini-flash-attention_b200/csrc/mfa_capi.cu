@@ -34,15 +34,15 @@ unsigned long long g_watchdog_ns = 2000000000ull;  // 2 s per wait
 
 // Two 128-row query tiles per CTA and a 3-slot K/V ring, except for D = 128, whose O would
 // not fit twice in TMEM next to S and P: one tile per CTA and a 2-slot ring (shared memory).
-template <bool kCausal, bool kBF16, int D = 64>
-using Full = FwdConfig<D == 128 ? 1 : 2, D == 128 ? 2 : 3, kCausal, kBF16, D>;
+template <bool kCausal, bool kBF16, int D = 64, bool kLSE = false>
+using Full = FwdConfig<D == 128 ? 1 : 2, D == 128 ? 2 : 3, kCausal, kBF16, D, kLSE>;
 template <bool kCausal>
 using Simple = FwdConfig<1, 2, kCausal, false, 64>;
 
 template <class Cfg>
 cudaError_t set_smem_attribute() {
   return cudaFuncSetAttribute(
-      mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim>,
+      mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim, Cfg::kLSE>,
       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
 }
 
@@ -65,12 +65,19 @@ cudaError_t set_bwd_attributes() {
   return e;
 }
 
+template <int D, bool kLSE>
+cudaError_t set_smem_attributes_dl() {
+  cudaError_t e = set_smem_attribute<Full<false, false, D, kLSE>>();
+  if (e == cudaSuccess) e = set_smem_attribute<Full<true, false, D, kLSE>>();
+  if (e == cudaSuccess) e = set_smem_attribute<Full<false, true, D, kLSE>>();
+  if (e == cudaSuccess) e = set_smem_attribute<Full<true, true, D, kLSE>>();
+  return e;
+}
+
 template <int D>
 cudaError_t set_smem_attributes_d() {
-  cudaError_t e = set_smem_attribute<Full<false, false, D>>();
-  if (e == cudaSuccess) e = set_smem_attribute<Full<true, false, D>>();
-  if (e == cudaSuccess) e = set_smem_attribute<Full<false, true, D>>();
-  if (e == cudaSuccess) e = set_smem_attribute<Full<true, true, D>>();
+  cudaError_t e = set_smem_attributes_dl<D, false>();
+  if (e == cudaSuccess) e = set_smem_attributes_dl<D, true>();
   return e;
 }
 
@@ -217,7 +224,7 @@ cudaError_t launch_merge(const MergeParams& mp, cudaStream_t stream) {
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg,
                             mfa_merge_kernel<Cfg::kRowsPerUnit, Cfg::kSlotFloats, Cfg::kCausal,
-                                             Cfg::kBF16, Cfg::kHeadDim>,
+                                             Cfg::kBF16, Cfg::kHeadDim, Cfg::kLSE>,
                             mp);
 }
 
@@ -290,7 +297,7 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
   p.status = status_ptr;
   p.workspace = workspace;
   p.lse = lse;
-  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim>
+  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim, Cfg::kLSE>
       <<<static_cast<unsigned>(pl.ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && pl.split) {
@@ -530,19 +537,30 @@ extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, v
 
 namespace mfa {
 namespace {
+template <int D, bool kLSE>
+int launch_general_l(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                     int64_t heads, int64_t n, float scale, int32_t causal, int32_t dtype,
+                     int32_t layout, cudaStream_t s, float* lse) {
+  if (dtype == MFA_DTYPE_BF16)
+    return causal ? launch_forward<Full<true, true, D, kLSE>>(q, k, v, out, batch, heads, n,
+                                                              layout, scale, s, lse)
+                  : launch_forward<Full<false, true, D, kLSE>>(q, k, v, out, batch, heads, n,
+                                                               layout, scale, s, lse);
+  return causal ? launch_forward<Full<true, false, D, kLSE>>(q, k, v, out, batch, heads, n,
+                                                             layout, scale, s, lse)
+                : launch_forward<Full<false, false, D, kLSE>>(q, k, v, out, batch, heads, n,
+                                                              layout, scale, s, lse);
+}
+
+// The row log-sum-exp is a compile-time option: the plain forward kernels carry none of it.
 template <int D>
 int launch_general(const void* q, const void* k, const void* v, void* out, int64_t batch,
                    int64_t heads, int64_t n, float scale, int32_t causal, int32_t dtype,
                    int32_t layout, cudaStream_t s, float* lse) {
-  if (dtype == MFA_DTYPE_BF16)
-    return causal ? launch_forward<Full<true, true, D>>(q, k, v, out, batch, heads, n, layout,
-                                                        scale, s, lse)
-                  : launch_forward<Full<false, true, D>>(q, k, v, out, batch, heads, n, layout,
-                                                         scale, s, lse);
-  return causal ? launch_forward<Full<true, false, D>>(q, k, v, out, batch, heads, n, layout,
-                                                       scale, s, lse)
-                : launch_forward<Full<false, false, D>>(q, k, v, out, batch, heads, n, layout,
-                                                        scale, s, lse);
+  return lse ? launch_general_l<D, true>(q, k, v, out, batch, heads, n, scale, causal, dtype,
+                                         layout, s, lse)
+             : launch_general_l<D, false>(q, k, v, out, batch, heads, n, scale, causal, dtype,
+                                          layout, s, nullptr);
 }
 
 int fwd_general(const void* q, const void* k, const void* v, void* out, float* lse,

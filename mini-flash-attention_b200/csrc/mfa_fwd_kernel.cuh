@@ -43,8 +43,9 @@
 
 namespace mfa {
 
-template <int NQ_, int STAGES_, bool CAUSAL_, bool BF16_, int D_>
+template <int NQ_, int STAGES_, bool CAUSAL_, bool BF16_, int D_, bool LSE_ = false>
 struct FwdConfig {
+  static constexpr bool kLSE = LSE_;  // also write the row log-sum-exp (FwdParams::lse)
   static constexpr int NQ = NQ_;
   static constexpr int STAGES = STAGES_;
   static constexpr bool kCausal = CAUSAL_;  // mask key index > query index
@@ -596,7 +597,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     tc_fence_before();
     const int b = cur.seg_idx & 1;
     if (cur.whole(p.sc)) {
-      if (p.lse != nullptr && q == 0) {
+      if (Cfg::kLSE && q == 0) {
         // log-sum-exp = ln 2 * (m + log2 l), m in scaled log2 units
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
@@ -674,10 +675,10 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   }
 }
 
-template <int NQ, int STAGES, bool CAUSAL, bool BF16, int D>
-__global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D>::kThreads, 1)
+template <int NQ, int STAGES, bool CAUSAL, bool BF16, int D, bool LSE>
+__global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::kThreads, 1)
     mfa_fwd_kernel(const __grid_constant__ FwdParams p) {
-  using Cfg = FwdConfig<NQ, STAGES, CAUSAL, BF16, D>;
+  using Cfg = FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -762,7 +763,7 @@ struct MergeParams {
 // grid has completed and its writes are visible.
 constexpr int kMergeThreadsPerRow = 4;
 
-template <int kRowsPerUnit, int kSlotFloats, bool kCausal, bool kBF16, int kD>
+template <int kRowsPerUnit, int kSlotFloats, bool kCausal, bool kBF16, int kD, bool kLSE>
 __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
     mfa_merge_kernel(const MergeParams mp) {
   constexpr int kChunks = kD / 4 / kMergeThreadsPerRow;  // float4 chunks per thread
@@ -815,7 +816,7 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   const int bh = u / mp.sc.q_blocks;
   const int qrow = (u % mp.sc.q_blocks) * kRowsPerUnit + r;
   if (qrow >= mp.n) return;
-  if (mp.lse != nullptr && k == 0)
+  if (kLSE && k == 0)
     mp.lse[static_cast<size_t>(bh) * mp.n + qrow] = (m_max + log2f(l)) * 0.6931471805599453f;
   const float inv_l = 1.0f / l;
   const long long offset = static_cast<long long>(bh / mp.heads) * mp.stride_b +
