@@ -169,9 +169,11 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- inputs
-def make_inputs(wl: dict, bh: int, seed: int, device) -> tuple:
-    """One buffer: q, k, v drawn in that order from one generator (benchmark_forward.py:222-227)."""
-    shape = (bh, wl["N"], D)
+def make_inputs(wl: dict, bh: int, seed: int, device, d: int = D, dtype=torch.float16,
+                with_grad: bool = False) -> tuple:
+    """One buffer: q, k, v drawn in that order from one generator (benchmark_forward.py:222-227),
+    then the output gradient dO when with_grad."""
+    shape = (bh, wl["N"], d)
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     if wl["dist"] == "uniform":
@@ -181,7 +183,11 @@ def make_inputs(wl: dict, bh: int, seed: int, device) -> tuple:
         q, k, v = (torch.randn(shape, device=device, generator=g, dtype=torch.float32)
                    for _ in range(3))
         q, k = q * wl["qk_scale"], k * wl["qk_scale"]
-    return q.half().contiguous(), k.half().contiguous(), v.half().contiguous()
+    out = [q.to(dtype).contiguous(), k.to(dtype).contiguous(), v.to(dtype).contiguous()]
+    if with_grad:
+        out.append(torch.randn(shape, device=device, generator=g, dtype=torch.float32)
+                   .to(dtype).contiguous())
+    return tuple(out)
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -273,12 +279,22 @@ def run_ours(args, wl) -> dict | None:
         shard = bh_shard(global_bh, rank, world)
     bh = shard.rows
     n = wl["N"]
-    inputs = [make_inputs(wl, bh, rank * INPUT_BUFFERS + i, dev) for i in range(INPUT_BUFFERS)]
+    d = args.head_dim
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    train = args.mode == "fwd_bwd"
+    inputs = [make_inputs(wl, bh, rank * INPUT_BUFFERS + i, dev, d, dtype, with_grad=train)
+              for i in range(INPUT_BUFFERS)]
     flush = torch.empty(L2_FLUSH_MB * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     causal = args.causal
 
-    def fwd(q, k, v):
-        return mfa.forward(q, k, v, causal=causal)
+    if train:
+        # one training step of the attention op: forward with its log-sum-exp, then backward
+        def fwd(q, k, v, do):
+            out, lse = mfa.forward_lse(q, k, v, causal=causal)
+            return mfa.backward(q, k, v, out, lse, do, causal=causal)
+    else:
+        def fwd(q, k, v):
+            return mfa.forward(q, k, v, causal=causal)
 
     stream = torch.cuda.current_stream(dev)
 
@@ -312,19 +328,23 @@ def run_ours(args, wl) -> dict | None:
 
         # ---- end to end: pinned host q, k, v -> device -> forward -> pinned host output,
         # through the public host-buffer API (copies of batch*head slices overlap kernels)
-        host_in = [x.cpu().pin_memory() for x in inputs[0]]
-        host_out = torch.empty(inputs[0][0].shape, dtype=torch.float16).pin_memory()
         e2e_steps = max(args.steps, 3)
-        chunks = min(bh, E2E_CHUNKS)
-        for _ in range(2):
-            mfa.forward_pinned(*host_in, causal=causal, out=host_out, chunks=chunks, device=dev)
-        torch.cuda.synchronize(dev)
-        barrier(world)
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            mfa.forward_pinned(*host_in, causal=causal, out=host_out, chunks=chunks, device=dev)
-        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
-        barrier(world)
+        e2e_ms = None
+        if not train:
+            host_in = [x.cpu().pin_memory() for x in inputs[0]]
+            host_out = torch.empty(inputs[0][0].shape, dtype=dtype).pin_memory()
+            chunks = min(bh, E2E_CHUNKS)
+            for _ in range(2):
+                mfa.forward_pinned(*host_in, causal=causal, out=host_out, chunks=chunks,
+                                   device=dev)
+            torch.cuda.synchronize(dev)
+            barrier(world)
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                mfa.forward_pinned(*host_in, causal=causal, out=host_out, chunks=chunks,
+                                   device=dev)
+            e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+            barrier(world)
 
     if world > 1:
         import torch.distributed as dist
@@ -333,17 +353,20 @@ def run_ours(args, wl) -> dict | None:
     if rank != 0:
         return None
 
-    flops_rank_step = attention_flops(bh, n, causal=causal)
-    job_flops_step = attention_flops(global_bh, n, causal=causal)
+    # a training step counts the forward (2 products) and the backward (5 products)
+    flop_mult = 3.5 if train else 1.0
+    flops_rank_step = flop_mult * attention_flops(bh, n, d, causal=causal)
+    job_flops_step = flop_mult * attention_flops(global_bh, n, d, causal=causal)
     value = job_flops_step * args.steps / (total_ms / 1e3) / 1e12
     kernel_ms = total_ms / args.steps
     achieved = flops_rank_step / (kernel_ms / 1e3) / 1e12
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    traffic = load_traffic("mfa_fwd", args.workload)
-    e2e_value = job_flops_step * e2e_steps / (e2e_ms / 1e3) / 1e12
-    bytes_in = 3 * global_bh * n * D * 2
-    bytes_out = global_bh * n * D * 2
+    default_mode = not train and d == D and dtype == torch.float16 and not causal
+    traffic = load_traffic("mfa_fwd", args.workload) if default_mode else None
+    e2e_value = None if e2e_ms is None else job_flops_step * e2e_steps / (e2e_ms / 1e3) / 1e12
+    bytes_in = 3 * global_bh * n * d * 2
+    bytes_out = global_bh * n * d * 2
     line = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -354,13 +377,13 @@ def run_ours(args, wl) -> dict | None:
         "ms_per_step": round(kernel_ms, 4),
         "higher_is_better": True,
         "scaling": wl["scaling"],
-        "vs_baseline": None if causal else round(value / PUBLISHED_TFLOPS, 2),
-        "dtype": "fp16",
+        "vs_baseline": round(value / PUBLISHED_TFLOPS, 2) if default_mode else None,
+        "dtype": args.dtype,
         "data": "synthetic (seeded, shapes and distributions of the workload; no dataset)",
         "config": {
             "workload": args.workload,
             "B": wl["B"] * (world if wl["scaling"] == "weak" else 1), "H": wl["H"], "N": n,
-            "D": D, "bh_per_gpu": bh, "causal": causal,
+            "D": d, "bh_per_gpu": bh, "causal": causal, "mode": args.mode,
             "parallelism": f"batch*head sharded over {world} GPU(s), no collective",
             "l2": f"{L2_FLUSH_MB} MB write before every step, outside the timed interval",
             "input_buffers": INPUT_BUFFERS,
@@ -375,25 +398,25 @@ def run_ours(args, wl) -> dict | None:
             "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4),
             "traffic": traffic,
-            "algorithmic_bytes": attention_bytes(bh, n),
+            "algorithmic_bytes": attention_bytes(bh, n, d),
             "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops burst)"
             if peak_src == "measured" else "fallback 1.59 PFLOP/s",
             "kernel": "mfa_fwd_kernel<2,3> (+ mfa_merge_kernel when the key dimension is split); "
                       "achieved = flops / CUDA-event time of the whole forward call",
         },
-        "e2e": {
+        "e2e": ({
             "value": round(e2e_value, 3), "unit": UNIT,
             "h2d_bytes_per_step": bytes_in, "d2h_bytes_per_step": bytes_out,
             "path": "mini_flash_attention.forward_pinned: pinned host q,k,v -> H2D / forward / "
                     "D2H of batch*head slices pipelined on 3 streams -> pinned host out",
             "timing": "host wall clock around the synchronous calls, max over ranks",
-        },
+        } if e2e_value is not None else {"value": None, "reason": "no host-buffer training API"}),
         "gpu_launches": None if per_call is None else per_call * args.steps,
         "gpu_kernels": kernel_names,
         "clocks": clocks,
         "wall_s_timed_region": round(wall, 4),
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and not train and d == D:
         line["cpu_baseline"] = cpu_baseline(wl, causal=causal)
     return line
 
@@ -479,6 +502,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-kernel", choices=["cpu", "cute"], default="cpu")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16")
+    ap.add_argument("--head-dim", type=int, choices=[32, 64, 128], default=D)
+    ap.add_argument("--mode", choices=["fwd", "fwd_bwd"], default="fwd",
+                    help="fwd: forward() (default); fwd_bwd: forward_lse + backward (D=64)")
     ap.add_argument("--causal", action="store_true",
                     help="mask key > query (flops counted over the N(N+1)/2 attended pairs)")
     ap.add_argument("--no-launch-count", action="store_true",
@@ -486,6 +513,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.mode == "fwd_bwd" and args.head_dim != 64:
+        ap.error("--mode fwd_bwd needs --head-dim 64 (the backward pass is D = 64)")
     wl = WORKLOADS[args.workload]
     line = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
     if line is not None:
