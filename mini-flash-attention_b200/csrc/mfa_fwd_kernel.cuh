@@ -756,17 +756,22 @@ struct MergeParams {
 
 // One CTA per forward CTA c; it merges the query block that starts inside c's range and
 // continues past it (if any): every piece's O is rescaled to the common row max, summed,
-// divided by the rescaled sum of row sums, rounded to fp16. Four threads per query row, each
-// on every fourth 16-byte chunk of it, so a warp reads 8 rows x 256 contiguous bytes.
-// Launched as a programmatic dependent of the forward kernel: the index work overlaps the
-// forward kernel's tail, and griddepcontrol.wait holds the workspace reads until the forward
-// grid has completed and its writes are visible.
+// divided by the rescaled sum of row sums, rounded to fp16 / bf16. Four threads per query
+// row, each on every fourth 16-byte chunk of it, so a warp reads 8 rows x 256 contiguous bytes.
+// Launched as a programmatic dependent of the forward kernel: all index work (which query
+// block, how many pieces, where the row goes) runs before griddepcontrol.wait and overlaps
+// the forward kernel's tail; after the wait the pieces are read two at a time for D <= 64
+// (one L2 round trip per pair; one at a time for D = 128, within the register budget) and
+// folded into a running max, sum and O.
 constexpr int kMergeThreadsPerRow = 4;
 
 template <int kRowsPerUnit, int kSlotFloats, bool kCausal, bool kBF16, int kD, bool kLSE>
 __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
     mfa_merge_kernel(const MergeParams mp) {
   constexpr int kChunks = kD / 4 / kMergeThreadsPerRow;  // float4 chunks per thread
+  constexpr int kOffM = kRowsPerUnit * kD;               // row maxima within a slot
+  constexpr int kOffL = kRowsPerUnit * (kD + 1);         // row sums within a slot
+  constexpr int kBatch = kChunks <= 4 ? 2 : 1;           // pieces read per round trip
   const int c = static_cast<int>(blockIdx.x);
   const long long total = mp.sc.total();
   long long b0, b1;
@@ -776,59 +781,91 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   const long long u0 = mp.sc.unit_first<kCausal>(u);
   const long long u1 = u0 + mp.sc.steps_of<kCausal>(u % mp.sc.q_blocks);
   // Merged here only if it starts inside c and ends past it.
-  const bool mine = b1 > b0 && u1 > b1 && u0 >= b0;
-  grid_dependency_wait();
-  if (!mine) return;
-  const int r = static_cast<int>(threadIdx.x) / kMergeThreadsPerRow;
-  const int k = static_cast<int>(threadIdx.x) % kMergeThreadsPerRow;
+  if (!(b1 > b0 && u1 > b1 && u0 >= b0)) {
+    grid_dependency_wait();
+    return;
+  }
   // Pieces: c's last segment (its first too if c's range starts exactly at u), then the
-  // first segment of every following CTA that overlaps u.
-  auto piece = [&](int cc) {
-    const int slot = cc == c ? (b0 == u0 ? 0 : 1) : 0;
-    return mp.workspace + static_cast<size_t>(2 * cc + slot) * kSlotFloats;
-  };
-  auto overlaps = [&](int cc) {
+  // first segment of every following CTA whose range starts before the query block ends.
+  int pieces = 1;
+  for (int cc = c + 1; cc < mp.ctas; ++cc) {
     long long s0, s1;
     split_range(total, cc, mp.ctas, s0, s1);
-    return cc < mp.ctas && s0 < u1;
-  };
-  float m_max = -INFINITY;
-  for (int cc = c; overlaps(cc); ++cc) m_max = fmaxf(m_max, piece(cc)[kRowsPerUnit * kD + r]);
-  float4 acc[kChunks];
-#pragma unroll
-  for (int i = 0; i < kChunks; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  float l = 0.0f;
-  for (int cc = c; overlaps(cc); ++cc) {
-    const float* ws = piece(cc);
-    // A piece whose keys are all masked for this row (causal) has m = -inf: weight 0.
-    const float w = ex2_approx(ws[kRowsPerUnit * kD + r] - m_max);
-    l += w * ws[kRowsPerUnit * (kD + 1) + r];
-    const float4* o = reinterpret_cast<const float4*>(ws + static_cast<size_t>(r) * kD);
-#pragma unroll
-    for (int i = 0; i < kChunks; ++i) {
-      const float4 v = o[kMergeThreadsPerRow * i + k];
-      acc[i].x += w * v.x;
-      acc[i].y += w * v.y;
-      acc[i].z += w * v.z;
-      acc[i].w += w * v.w;
-    }
+    if (s0 >= u1) break;
+    ++pieces;
   }
+  const int r = static_cast<int>(threadIdx.x) / kMergeThreadsPerRow;
+  const int k = static_cast<int>(threadIdx.x) % kMergeThreadsPerRow;
   const int bh = u / mp.sc.q_blocks;
   const int qrow = (u % mp.sc.q_blocks) * kRowsPerUnit + r;
-  if (qrow >= mp.n) return;
-  if (kLSE && k == 0)
-    mp.lse[static_cast<size_t>(bh) * mp.n + qrow] = (m_max + log2f(l)) * 0.6931471805599453f;
-  const float inv_l = 1.0f / l;
   const long long offset = static_cast<long long>(bh / mp.heads) * mp.stride_b +
                            static_cast<long long>(bh % mp.heads) * mp.stride_h +
                            static_cast<long long>(qrow) * mp.stride_n;
+  // Slot of piece i: CTA c's second slot unless its range starts at u; slot 0 of the others.
+  const float* first = mp.workspace + static_cast<size_t>(2 * c + (b0 == u0 ? 0 : 1)) * kSlotFloats;
+  auto piece = [&](int i) {
+    return i == 0 ? first : mp.workspace + static_cast<size_t>(2 * (c + i)) * kSlotFloats;
+  };
+  grid_dependency_wait();
+  if (qrow >= mp.n) return;
+
+  // Piece 0 holds key block 0, so its row max is finite for every row (causal included) and
+  // the running max is finite from the first pair on; a fully masked later piece has
+  // m = -inf and weight 0.
+  float m_run = -INFINITY, l = 0.0f;
+  float4 acc[kChunks];
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < pieces; i += kBatch) {
+    float m[kBatch], ls[kBatch];
+    float4 o[kBatch][kChunks];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      // a missing last piece of the batch re-reads piece i with m = -inf, i.e. weight 0
+      const bool here = i + b < pieces;
+      const float* ws = piece(here ? i + b : i);
+      m[b] = here ? ws[kOffM + r] : -INFINITY;
+      ls[b] = ws[kOffL + r];
+      const float4* src = reinterpret_cast<const float4*>(ws + static_cast<size_t>(r) * kD);
+#pragma unroll
+      for (int q = 0; q < kChunks; ++q) o[b][q] = src[kMergeThreadsPerRow * q + k];
+    }
+    float m_new = m_run;
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) m_new = fmaxf(m_new, m[b]);
+    const float s = ex2_approx(m_run - m_new);  // 0 on the first batch (m_run = -inf)
+    l *= s;
+#pragma unroll
+    for (int q = 0; q < kChunks; ++q) {
+      acc[q].x *= s;
+      acc[q].y *= s;
+      acc[q].z *= s;
+      acc[q].w *= s;
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const float w = ex2_approx(m[b] - m_new);
+      l += w * ls[b];
+#pragma unroll
+      for (int q = 0; q < kChunks; ++q) {
+        acc[q].x += w * o[b][q].x;
+        acc[q].y += w * o[b][q].y;
+        acc[q].z += w * o[b][q].z;
+        acc[q].w += w * o[b][q].w;
+      }
+    }
+    m_run = m_new;
+  }
+  if (kLSE && k == 0)
+    mp.lse[static_cast<size_t>(bh) * mp.n + qrow] = (m_run + log2f(l)) * 0.6931471805599453f;
+  const float inv_l = 1.0f / l;
   uint2* dst = reinterpret_cast<uint2*>(static_cast<uint16_t*>(mp.out) + offset);
 #pragma unroll
-  for (int i = 0; i < kChunks; ++i) {
+  for (int q = 0; q < kChunks; ++q) {
     uint2 w;
-    w.x = pack_pair<kBF16>(acc[i].x * inv_l, acc[i].y * inv_l);
-    w.y = pack_pair<kBF16>(acc[i].z * inv_l, acc[i].w * inv_l);
-    dst[kMergeThreadsPerRow * i + k] = w;
+    w.x = pack_pair<kBF16>(acc[q].x * inv_l, acc[q].y * inv_l);
+    w.y = pack_pair<kBF16>(acc[q].z * inv_l, acc[q].w * inv_l);
+    dst[kMergeThreadsPerRow * q + k] = w;
   }
 }
 
