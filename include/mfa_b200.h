@@ -42,8 +42,9 @@ enum mfa_status_code {
  * (src/mini_flash_attention/flash_attn_cuda.cu:370-420): same arguments, the same D == 64 check
  * and message; any N >= 1 (the reference requires N % 128 == 0, flash_attn_cuda.cu:402-407).
  * `scale` multiplies q.k before the softmax (the reference binding passes 1/sqrt(D),
- * flash_attn.cpp:94). q, k, v and out must be memory of the current device (checked: other
- * pointers return MFA_ERR_INVALID_ARGUMENT before any launch). causal != 0 masks
+ * flash_attn.cpp:94); it must be positive and finite (MFA_ERR_INVALID_ARGUMENT otherwise).
+ * q, k, v and out must be memory of the current device (checked: other pointers return
+ * MFA_ERR_INVALID_ARGUMENT before any launch). causal != 0 masks
  * key index > query index (the reference launcher rejects causal, flash_attn_cuda.cu:408-410;
  * the mask is the one its test and benchmark build, tests/test_forward.py:30-32).
  * bh == 0 or n == 0 is a no-op that returns MFA_OK.

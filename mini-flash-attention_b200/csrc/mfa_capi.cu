@@ -512,7 +512,8 @@ extern "C" int mfa_fwd_f16(const void* q, const void* k, const void* v, void* ou
   // the last key block masks keys past N and the stores clip rows past N), and so is causal
   // masking (rejected by flash_attn_cuda.cu:408-410).
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
-  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  if (!(scale > 0.0f) || !std::isfinite(scale))
+    return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be positive and finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return causal ? launch_forward<Full<true, false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s)
                 : launch_forward<Full<false, false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale,
@@ -529,7 +530,8 @@ extern "C" int mfa_fwd_simple_f16(const void* q, const void* k, const void* v, v
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This WMMA prototype supports only D=64 yet");
   if (n % 64 != 0)
     return fail(MFA_ERR_SEQ_LEN, "Only N (seq len) divisible by 64 and 64 are supported yet");
-  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  if (!(scale > 0.0f) || !std::isfinite(scale))
+    return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be positive and finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return causal ? launch_forward<Simple<true>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s)
                 : launch_forward<Simple<false>>(q, k, v, out, 1, bh, n, MFA_LAYOUT_BHND, scale, s);
@@ -577,7 +579,8 @@ int fwd_general(const void* q, const void* k, const void* v, void* out, float* l
     return fail(MFA_ERR_INVALID_ARGUMENT, "dtype must be MFA_DTYPE_FP16 or MFA_DTYPE_BF16");
   if (layout != MFA_LAYOUT_BHND && layout != MFA_LAYOUT_BNHD)
     return fail(MFA_ERR_INVALID_ARGUMENT, "layout must be MFA_LAYOUT_BHND or MFA_LAYOUT_BNHD");
-  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  if (!(scale > 0.0f) || !std::isfinite(scale))
+    return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be positive and finite");
   if (batch * heads > 0 && n > 0 && lse != nullptr) {
     if (reinterpret_cast<uintptr_t>(lse) & 3u)
       return fail(MFA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
@@ -709,7 +712,8 @@ extern "C" int mfa_bwd(const void* q, const void* k, const void* v, const void* 
     return fail(MFA_ERR_INVALID_ARGUMENT, "dtype must be MFA_DTYPE_FP16 or MFA_DTYPE_BF16");
   if (layout != MFA_LAYOUT_BHND && layout != MFA_LAYOUT_BNHD)
     return fail(MFA_ERR_INVALID_ARGUMENT, "layout must be MFA_LAYOUT_BHND or MFA_LAYOUT_BNHD");
-  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  if (!(scale > 0.0f) || !std::isfinite(scale))
+    return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be positive and finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == MFA_DTYPE_BF16)
     return causal ? launch_backward<true, true>(q, k, v, out, dout, lse, dq, dk, dv, batch,
@@ -728,7 +732,8 @@ extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, 
   int rc = check_common(q, k, v, out, bh, n, d);
   if (rc != MFA_OK) return rc;
   if (d != 64) return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=64");
-  if (!std::isfinite(scale)) return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be finite");
+  if (!(scale > 0.0f) || !std::isfinite(scale))
+    return fail(MFA_ERR_INVALID_ARGUMENT, "scale must be positive and finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return causal ? launch_forward_noalloc<Full<true, false>>(q, k, v, out, bh, n, scale, s)
                 : launch_forward_noalloc<Full<false, false>>(q, k, v, out, bh, n, scale, s);

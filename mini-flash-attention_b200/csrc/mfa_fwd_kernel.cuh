@@ -459,9 +459,8 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
     }
   }
 
-  // Row maxima: two 3-input max chains per row over this thread's 32 scores, then the row's
-  // four threads combine theirs.
-  float mrow[2];
+  // This thread's row maxima: two 3-input max chains per row over its 32 scores.
+  float mloc[2];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     float a = fmaxf(f(sr[2 * r]), f(sr[2 * r + 1]));
@@ -471,34 +470,35 @@ __device__ __forceinline__ bool softmax_step(const FwdParams& p, uint32_t bars, 
       a = max3(a, f(sr[4 * i + 2 * r]), f(sr[4 * i + 2 * r + 1]));
       b = max3(b, f(sr[4 * i + 4 + 2 * r]), f(sr[4 * i + 5 + 2 * r]));
     }
-    mrow[r] = fmaxf(a, b);
+    mloc[r] = fmaxf(a, b);
   }
+  // The reference max is raised only when some row of the warp grew past the threshold. A
+  // row grows iff one of its four threads holds a score past it (c > 0: scaling preserves
+  // the order), so the vote runs on the thread maxima and the row maxima are combined by
+  // shuffles only on that rare path; otherwise the reference max stays and alpha = 1.
+  const bool grow = __any_sync(0xffffffffu, mloc[0] * c > m_run[0] + Cfg::kRescaleThreshold ||
+                                                mloc[1] * c > m_run[1] + Cfg::kRescaleThreshold);
+  float alpha[2] = {1.0f, 1.0f};
+  if (grow) {
 #pragma unroll
-  for (int r = 0; r < 2; ++r) mrow[r] = fmaxf(mrow[r], __shfl_xor_sync(0xffffffffu, mrow[r], 1));
+    for (int r = 0; r < 2; ++r) mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(0xffffffffu, mloc[r], 1));
 #pragma unroll
-  for (int r = 0; r < 2; ++r) mrow[r] = fmaxf(mrow[r], __shfl_xor_sync(0xffffffffu, mrow[r], 2));
-  float m_new[2];
+    for (int r = 0; r < 2; ++r) mloc[r] = fmaxf(mloc[r], __shfl_xor_sync(0xffffffffu, mloc[r], 2));
 #pragma unroll
-  for (int r = 0; r < 2; ++r) m_new[r] = fmaxf(m_run[r], mrow[r] * c);
-  // Raise the reference max only when some row of the warp grew past the threshold; the
-  // four threads of a row hold the same maxima, so they take the same decision.
-  const bool grow = __any_sync(0xffffffffu, m_new[0] > m_run[0] + Cfg::kRescaleThreshold ||
-                                                m_new[1] > m_run[1] + Cfg::kRescaleThreshold);
-  float alpha[2];
+    for (int r = 0; r < 2; ++r) {
+      const float m_use = fmaxf(m_run[r], mloc[r] * c);
+      // 0 on a unit's first block (m_run = -inf); 1 while every key so far is masked
+      // (causal, m_use = -inf), without an -inf - -inf
+      if (!(Cfg::kCausal && m_use == -INFINITY)) alpha[r] = ex2_approx(m_run[r] - m_use);
+      m_run[r] = m_use;
+    }
+  }
   uint64_t negm2[2];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
-    const float m_use = grow ? m_new[r] : m_run[r];
-    if (Cfg::kCausal && m_use == -INFINITY) {
-      // every key so far is masked for this row (possible in a piece of a query block):
-      // O and the row sum are still zero, and p = 2^(-inf) = 0 without an -inf - -inf
-      alpha[r] = 1.0f;
-      negm2[r] = f2_splat(0.0f);
-    } else {
-      alpha[r] = ex2_approx(m_run[r] - m_use);  // 0 on a unit's first block (m_run = -inf)
-      negm2[r] = f2_splat(-m_use);
-    }
-    m_run[r] = m_use;
+    // every key so far masked for this row (causal, possible in a piece of a query block):
+    // O and the row sum are still zero, and p = 2^(-inf - 0) = 0
+    negm2[r] = f2_splat(Cfg::kCausal && m_run[r] == -INFINITY ? 0.0f : -m_run[r]);
   }
 
   // Scale-subtract and row sums run on packed pairs (fma/add .f32x2); pair k is row k % 2.

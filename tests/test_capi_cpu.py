@@ -125,6 +125,17 @@ def test_empty_problem_is_a_noop():
     capi.fwd(0, 0, 0, 0, 4, 0, 64, 0.125, simple=True)
 
 
+@pytest.mark.parametrize("scale", [0.0, -0.125, float("nan"), float("inf")])
+def test_scale_must_be_positive_and_finite(scale):
+    # the kernels' row-max logic relies on scale > 0; rejected before any device access
+    for call in (lambda: capi.fwd(FAKE, FAKE, FAKE, FAKE, 2, 256, 64, scale),
+                 lambda: capi.fwd_general(FAKE, FAKE, FAKE, FAKE, 1, 2, 256, 64, scale)):
+        with pytest.raises(capi.MfaError) as e:
+            call()
+        assert e.value.code == capi.MFA_ERR_INVALID_ARGUMENT
+        assert str(e.value) == "scale must be positive and finite"
+
+
 def test_watchdog_limit_validated():
     with pytest.raises(capi.MfaError) as e:
         capi.set_watchdog_ns(10)
