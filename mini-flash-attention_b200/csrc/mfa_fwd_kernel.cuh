@@ -21,6 +21,8 @@
 //                     MN-major, so no transpose).
 //   warp  8*NQ+1    : TMA producer: the Q tiles of each unit (two Q buffers, so the next
 //                     unit's Q loads while this one runs), then K and V blocks.
+//   warp  8*NQ+2    : (NQ = 2) TMA stores of finished units' output (staged in their Q
+//                     buffer), so the softmax warps go on to the next unit without waiting.
 // TMEM columns: S_i at 128*i, P_i (fp16 pairs) at 128*NQ + 64*i, O_i at 192*NQ + 64*i.
 // exp is exp2 with scale*log2(e) folded into one FMA; 1 of every 8 pairs uses an FMA-pipe
 // polynomial instead of MUFU. The running max is only raised when it grows by more than
@@ -66,10 +68,16 @@ struct FwdConfig {
   static constexpr int kSoftmaxWarps = 8 * NQ;   // two warps per TMEM lane quadrant and tile
   static constexpr int kMmaWarp = kSoftmaxWarps;
   static constexpr int kLoadWarp = kSoftmaxWarps + 1;
+  // Output stores of finished units: a store warp with two query tiles (it fills the fifth
+  // warpgroup, otherwise idle); with one tile the first softmax warp of the tile issues them
+  // (a third non-softmax warp next to two softmax warps per sub-partition measured slower).
+  static constexpr bool kStoreRole = NQ == 2;
+  static constexpr int kStoreWarp = kSoftmaxWarps + 2;
   // With two query tiles (16 softmax warps) the register file is rebalanced with setmaxnreg,
-  // which works per warpgroup: the MMA and TMA warps then fill a fifth warpgroup (2 warps
-  // idle). 640 threads launch with 96 registers each (5 warps per SM sub-partition); after
-  // the split: 512 x 104 + 128 x 64 = 640 x 96, and per sub-partition 4 x 104 + 64 <= 512.
+  // which works per warpgroup: the MMA, load and store warps then fill a fifth warpgroup
+  // (1 warp idle). 640 threads launch with 96 registers each (5 warps per SM
+  // sub-partition); after the split: 512 x 104 + 128 x 64 = 640 x 96, and per sub-partition
+  // 4 x 104 + 64 <= 512.
   static constexpr bool kRebalanceRegs = NQ == 2;
   static constexpr int kThreads = kRebalanceRegs ? 32 * 20 : 32 * (kSoftmaxWarps + 2);
   static constexpr int kLaunchRegs = 96;
@@ -567,8 +575,8 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
   const uint32_t tO = tmem + lane_bits + Cfg::kColO + Cfg::kHeadDim * tile;
   const bool tile_leader = (warp & 7) == 0 && lane == 0;
 
-  int g = 0;       // global step index (phase of the per-step barriers)
-  int stores = 0;  // whole units stored so far (phase of the staging barrier)
+  int g = 0;  // global step index (phase of the per-step barriers)
+  [[maybe_unused]] int stores = 0;  // whole units stored (staging phase; no store warp)
   StepCursor<Cfg::kCausal> cur;
   cur.init(p);
   while (cur.valid()) {
@@ -630,25 +638,27 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(Cfg::kBarStage + tile));
-      if (tile_leader) {
-        // the tile's eight warps have written their staging rows: store, then free the
-        // Q buffer once the store has read it
-        if (!wait_single(bar(Cfg::kBarStage + tile), static_cast<uint32_t>(stores) & 1u, wd,
-                         kSiteSoftStage))
-          return;
-        const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
-        if (r0 < p.n) {
-          const HeadBatch ob = head_batch(p, cur.u);
+      if constexpr (!Cfg::kStoreRole) {
+        // no store warp: the tile's first warp stores once all eight have written their
+        // staging rows, then frees the Q buffer when the store has read it
+        if (tile_leader) {
+          if (!wait_single(bar(Cfg::kBarStage + tile), static_cast<uint32_t>(stores) & 1u, wd,
+                           kSiteSoftStage))
+            return;
+          const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
+          if (r0 < p.n) {
+            const HeadBatch ob = head_batch(p, cur.u);
 #pragma unroll
-          for (int x = 0; x < Cfg::kBoxes; ++x)
-            tma_store_4d(&p.tm_o, smem_addr(stage + x * Cfg::kBoxBytes), x * Cfg::kBoxCols, r0,
-                         ob.h, ob.b);
-          tma_store_commit();
-          tma_store_wait_read();
+            for (int x = 0; x < Cfg::kBoxes; ++x)
+              tma_store_4d(&p.tm_o, smem_addr(stage + x * Cfg::kBoxBytes), x * Cfg::kBoxCols,
+                           r0, ob.h, ob.b);
+            tma_store_commit();
+            tma_store_wait_read();
+          }
+          mbar_arrive(bar(Cfg::kBarQEmpty + b));
         }
-        mbar_arrive(bar(Cfg::kBarQEmpty + b));
+        ++stores;
       }
-      ++stores;
     } else {
       // A piece of a query block: unnormalised O, the row max and the row sum go to this
       // CTA's workspace slot (first or last segment of its range) for the merge kernel.
@@ -673,6 +683,51 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     }
     cur.next_segment(p);
   }
+}
+
+// One thread of the store warp: once the eight softmax warps of a tile have written its
+// normalised output into the staging buffer (the unit's Q buffer), store it with TMA, and
+// free the Q buffer for the load warp when the stores have read it. Keeping the store's
+// issue and read wait here leaves the softmax warps free to start the next unit.
+template <class Cfg>
+__device__ __forceinline__ void store_role(const FwdParams& p, uint8_t* smem, uint32_t bars,
+                                           const Watchdog& wd) {
+  auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
+  StepCursor<Cfg::kCausal> cur;
+  cur.init(p);
+  int stores = 0;  // whole units stored so far (phase of the staging barriers)
+  while (cur.valid()) {
+    if (cur.whole(p.sc)) {
+      const int b = cur.seg_idx & 1;
+      const HeadBatch ob = head_batch(p, cur.u);
+      bool ok = true;
+#pragma unroll
+      for (int tile = 0; tile < Cfg::NQ; ++tile) {
+        if (!wait_single(bar(Cfg::kBarStage + tile), static_cast<uint32_t>(stores) & 1u, wd,
+                         kSiteSoftStage)) {
+          ok = false;
+          break;
+        }
+        const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
+        if (r0 < p.n) {
+          const uint32_t stage =
+              smem_addr(smem + Cfg::kQOff + (b * Cfg::NQ + tile) * Cfg::kTileBytes);
+#pragma unroll
+          for (int x = 0; x < Cfg::kBoxes; ++x)
+            tma_store_4d(&p.tm_o, stage + x * Cfg::kBoxBytes, x * Cfg::kBoxCols, r0, ob.h, ob.b);
+        }
+      }
+      tma_store_commit();
+      if (!ok) break;
+      tma_store_wait_read();
+#pragma unroll
+      for (int tile = 0; tile < Cfg::NQ; ++tile) mbar_arrive(bar(Cfg::kBarQEmpty + b));
+      ++stores;
+    }
+    cur.next_segment(p);
+  }
+  // Unwinding or done: shared memory must outlive every store's read of it.
+  tma_store_wait_read();
 }
 
 template <int NQ, int STAGES, bool CAUSAL, bool BF16, int D, bool LSE>
@@ -730,6 +785,8 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
       if (lane == 0) load_role<Cfg>(p, smem, bars, wd);
     } else if (warp == Cfg::kMmaWarp) {
       mma_role<Cfg>(p, smem, bars, tmem, wd);
+    } else if (Cfg::kStoreRole && warp == Cfg::kStoreWarp) {
+      if (lane == 0) store_role<Cfg>(p, smem, bars, wd);
     }
   } else {
     if constexpr (Cfg::kRebalanceRegs) setmaxnreg_inc<Cfg::kSoftmaxRegs>();
