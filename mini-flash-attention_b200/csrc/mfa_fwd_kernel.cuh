@@ -191,7 +191,7 @@ struct StepCursor {
   __device__ void step(const FwdParams& p) {
     if (++j >= j1 && rem > 0) {
       if (p.split) {
-        ++u;
+        u = p.sc.next_unit<kCausal>(u);
         const int steps = p.sc.steps_of<kCausal>(u % p.sc.q_blocks);
         j1 = rem < steps ? rem : steps;
         rem -= j1;

@@ -2,13 +2,17 @@
 // and the merge kernel (device).
 //
 // A step is one key block (128 keys) of one query block (rows_per_unit query rows) of one
-// (batch * head) row. Steps are numbered row-major over (head, query block, key block). Without
-// causal masking every query block has nkb = ceil(N / 128) steps. With causal masking (key
+// (batch * head) row; a unit is one query block of one head, u = head * q_blocks + qb. Steps
+// are numbered head-major and, within a head, query block by query block in the head's
+// processing order, key blocks ascending. Without causal masking every query block has
+// nkb = ceil(N / 128) steps and the order is qb = 0, 1, 2, ... With causal masking (key
 // index > query index masked, as the reference's test and benchmark build the mask,
 // tests/test_forward.py:30-32 and benchs/benchmark_forward.py:109-112) query block qb needs
-// only the key blocks that start at or before its last row: min(nkb, group * (qb + 1)) with
-// group = rows_per_unit / 128, so a head's steps form a triangle and a step's query block is
-// found from the inverse triangular number.
+// only the key blocks that start at or before its last row: group * (qb + 1) with group =
+// rows_per_unit / 128, nkb for the last block. Its order pairs short and long blocks,
+// qb = 0, Q-1, 1, Q-2, ... (Q = q_blocks): every pair after the first has group * (Q + 1)
+// steps, so an even split of the steps gives every CTA about the same number of query
+// blocks, i.e. of unit epilogues and diagonal (masked) blocks, and a step is located in O(1).
 #pragma once
 
 #include <cmath>
@@ -29,21 +33,46 @@ struct Schedule {
   template <bool kCausal>
   __host__ __device__ int steps_of(int qb) const {
     if (!kCausal) return nkb;
-    const int need = (qb + 1) * group;
-    return need < nkb ? need : nkb;
+    // only the last query block can reach past key block nkb - 1 (it holds row N - 1)
+    return qb == q_blocks - 1 ? nkb : (qb + 1) * group;
   }
-  // First step of query block qb inside its head. Only the last query block can be capped by
-  // nkb (every earlier block ends before row N), so the triangular sum is exact for all qb.
+  // Causal order: query block at position k of its head, and the position of query block qb.
+  __host__ __device__ int qb_at(int k) const {
+    return (k & 1) ? q_blocks - 1 - (k >> 1) : (k >> 1);
+  }
+  __host__ __device__ int pos_of(int qb) const {
+    return 2 * qb < q_blocks ? 2 * qb : 2 * (q_blocks - 1 - qb) + 1;
+  }
+  // Causal: steps of the first pair (query blocks 0 and Q-1) and of every later pair.
+  __host__ __device__ long long pair0() const { return static_cast<long long>(group) + nkb; }
+  __host__ __device__ long long pair_steps() const {
+    return static_cast<long long>(group) * (q_blocks + 1);
+  }
+  // Causal: first step (within its head) of the query block at position k.
+  __host__ __device__ long long pos_first(int k) const {
+    const int m = k >> 1;
+    long long f = m == 0 ? 0 : pair0() + (m - 1) * pair_steps();
+    if (k & 1) f += steps_of<true>(m);
+    return f;
+  }
+  // First step of query block qb inside its head.
   template <bool kCausal>
   __host__ __device__ long long first_of(int qb) const {
-    return kCausal ? static_cast<long long>(group) * qb * (qb + 1) / 2
-                   : static_cast<long long>(qb) * nkb;
+    return kCausal ? pos_first(pos_of(qb)) : static_cast<long long>(qb) * nkb;
   }
   __host__ __device__ long long total() const { return head_steps * bh; }
-  // First global step of unit u (row-major over (head, query block)).
+  // First global step of unit u.
   template <bool kCausal>
   __host__ __device__ long long unit_first(int u) const {
     return static_cast<long long>(u / q_blocks) * head_steps + first_of<kCausal>(u % q_blocks);
+  }
+  // The unit processed after unit u (in split mode, where a CTA walks consecutive steps).
+  template <bool kCausal>
+  __host__ __device__ int next_unit(int u) const {
+    if (!kCausal) return u + 1;
+    const int head = u / q_blocks;
+    const int k = pos_of(u - head * q_blocks) + 1;
+    return k < q_blocks ? head * q_blocks + qb_at(k) : (head + 1) * q_blocks;
   }
   // Unit u and key block j of global step s (0 <= s < total()).
   template <bool kCausal>
@@ -56,17 +85,30 @@ struct Schedule {
     }
     const long long head = s / head_steps;
     const long long r = s - head * head_steps;
-    int qb;
-    {
-      // largest qb with group * qb * (qb + 1) / 2 <= r, from the float root and corrected
-      qb = static_cast<int>((sqrtf(8.0f * static_cast<float>(r) / group + 1.0f) - 1.0f) * 0.5f);
-      if (qb > q_blocks - 1) qb = q_blocks - 1;
-      if (qb < 0) qb = 0;
-      while (qb + 1 < q_blocks && first_of<kCausal>(qb + 1) <= r) ++qb;
-      while (qb > 0 && first_of<kCausal>(qb) > r) --qb;
+    const int pairs = q_blocks >> 1;
+    int k;
+    long long rem;
+    if (pairs > 0 && r < pair0()) {
+      k = 0;
+      rem = r;
+    } else if (pairs > 1 && r < pair0() + (pairs - 1) * pair_steps()) {
+      const long long t = r - pair0();
+      const long long m = 1 + t / pair_steps();
+      k = static_cast<int>(2 * m);
+      rem = t - (m - 1) * pair_steps();
+    } else {  // the middle query block of an odd count, alone at the last position
+      k = q_blocks - 1;
+      rem = r - pos_first(k);
     }
-    u = static_cast<int>(head * q_blocks + qb);
-    j = static_cast<int>(r - first_of<kCausal>(qb));
+    if (!(k & 1) && k + 1 < q_blocks) {  // a pair: the short block, then the long one
+      const int s_even = steps_of<true>(k >> 1);
+      if (rem >= s_even) {
+        ++k;
+        rem -= s_even;
+      }
+    }
+    u = static_cast<int>(head * q_blocks + qb_at(k));
+    j = static_cast<int>(rem);
   }
 };
 
@@ -78,7 +120,7 @@ inline Schedule make_schedule(long long bh, long long n, int rows_per_unit, int 
   s.nkb = static_cast<int>((n + keys_per_block - 1) / keys_per_block);
   s.group = rows_per_unit / keys_per_block;
   s.causal = causal ? 1 : 0;
-  s.head_steps = causal ? s.first_of<true>(s.q_blocks - 1) + s.steps_of<true>(s.q_blocks - 1)
+  s.head_steps = causal ? s.pos_first(s.q_blocks - 1) + s.steps_of<true>(s.qb_at(s.q_blocks - 1))
                        : s.first_of<false>(s.q_blocks - 1) + s.steps_of<false>(s.q_blocks - 1);
   return s;
 }

@@ -4,10 +4,12 @@ csrc/mfa_schedule.cuh (Schedule: steps_of, first_of, locate; split_range), csrc/
 csrc/mfa_capi.cu). Checked, with and without causal masking: every (query block, key block)
 step that the mask needs is processed exactly once, every partial piece lands in its own
 workspace slot, and every query block cut into pieces is merged exactly once from exactly its
-pieces."""
+pieces. With causal masking the query blocks of a head run in the order 0, Q-1, 1, Q-2, ...
+(pairs of short and long blocks), which spreads unit epilogues and diagonal blocks evenly over
+the CTAs; the brute force below walks the steps in that order and is checked against the
+O(1) locate of the kernels."""
 from __future__ import annotations
 
-import math
 
 import pytest
 
@@ -19,13 +21,33 @@ class Schedule:
         self.nkb = -(-n // keys)
         self.group = rows_per_unit // keys
         self.causal = causal
-        self.head_steps = self.first_of(self.q_blocks - 1) + self.steps_of(self.q_blocks - 1)
+        self.head_steps = sum(self.steps_of(qb) for qb in range(self.q_blocks))
 
     def steps_of(self, qb):
-        return min(self.nkb, (qb + 1) * self.group) if self.causal else self.nkb
+        if not self.causal:
+            return self.nkb
+        return self.nkb if qb == self.q_blocks - 1 else (qb + 1) * self.group
+
+    # causal processing order within a head: position k holds query block qb_at(k)
+    def qb_at(self, k):
+        return self.q_blocks - 1 - k // 2 if k % 2 else k // 2
+
+    def pos_of(self, qb):
+        return 2 * qb if 2 * qb < self.q_blocks else 2 * (self.q_blocks - 1 - qb) + 1
+
+    def order(self):
+        """Query blocks of a head in processing order (brute force)."""
+        return [self.qb_at(k) for k in range(self.q_blocks)] if self.causal \
+            else list(range(self.q_blocks))
+
+    def pos_first(self, k):
+        pair0, pair = self.group + self.nkb, self.group * (self.q_blocks + 1)
+        m = k // 2
+        f = 0 if m == 0 else pair0 + (m - 1) * pair
+        return f + (self.steps_of(m) if k % 2 else 0)
 
     def first_of(self, qb):
-        return self.group * qb * (qb + 1) // 2 if self.causal else qb * self.nkb
+        return self.pos_first(self.pos_of(qb)) if self.causal else qb * self.nkb
 
     def total(self):
         return self.head_steps * self.bh
@@ -33,18 +55,32 @@ class Schedule:
     def unit_first(self, u):
         return u // self.q_blocks * self.head_steps + self.first_of(u % self.q_blocks)
 
+    def next_unit(self, u):
+        if not self.causal:
+            return u + 1
+        head, qb = divmod(u, self.q_blocks)
+        k = self.pos_of(qb) + 1
+        return head * self.q_blocks + self.qb_at(k) if k < self.q_blocks \
+            else (head + 1) * self.q_blocks
+
     def locate(self, s):
         head, r = divmod(s, self.head_steps)
         if not self.causal:
-            qb = r // self.nkb
+            return head * self.q_blocks + r // self.nkb, r % self.nkb
+        pairs = self.q_blocks // 2
+        pair0, pair = self.group + self.nkb, self.group * (self.q_blocks + 1)
+        if pairs > 0 and r < pair0:
+            k, rem = 0, r
+        elif pairs > 1 and r < pair0 + (pairs - 1) * pair:
+            m = 1 + (r - pair0) // pair
+            k, rem = 2 * m, r - pair0 - (m - 1) * pair
         else:
-            qb = int((math.sqrt(8.0 * r / self.group + 1.0) - 1.0) * 0.5)
-            qb = max(0, min(qb, self.q_blocks - 1))
-            while qb + 1 < self.q_blocks and self.first_of(qb + 1) <= r:
-                qb += 1
-            while qb > 0 and self.first_of(qb) > r:
-                qb -= 1
-        return head * self.q_blocks + qb, r - self.first_of(qb)
+            k = self.q_blocks - 1
+            rem = r - self.pos_first(k)
+        if k % 2 == 0 and k + 1 < self.q_blocks and rem >= self.steps_of(k // 2):
+            rem -= self.steps_of(k // 2)
+            k += 1
+        return head * self.q_blocks + self.qb_at(k), rem
 
 
 def split_range(total, cta, ctas):
@@ -74,9 +110,11 @@ def segments(sc, split, cta, ctas):
         return
     b, e = split_range(sc.total(), cta, ctas)
     steps = []
-    for u in range(units):
-        for j in range(sc.steps_of(u % sc.q_blocks)):
-            steps.append((u, j))
+    for head in range(sc.bh):
+        for qb in sc.order():
+            u = head * sc.q_blocks + qb
+            for j in range(sc.steps_of(qb)):
+                steps.append((u, j))
     mine = steps[b:e]
     first = True
     i = 0
@@ -115,7 +153,7 @@ def cursor_segments(sc, split, cta, ctas):
         yield u, j0, j1, seg == 0
         if rem <= 0:
             return
-        u += 1
+        u = sc.next_unit(u)
         j0, j1 = 0, min(rem, sc.steps_of(u % sc.q_blocks))
         rem -= j1
         seg += 1
@@ -191,14 +229,30 @@ def test_every_step_once_and_pieces_merged_once(bh, n, rows, sms, causal):
 
 
 @pytest.mark.parametrize("bh,n,rows", [(1, 4096, 256), (3, 384, 256), (2, 1 << 20, 256),
-                                       (1, 640, 128), (5, 32768, 256)])
-def test_locate_inverts_the_triangle(bh, n, rows):
+                                       (1, 640, 128), (5, 32768, 256), (2, 256, 256),
+                                       (2, 257, 256), (3, 640, 256), (1, 129, 128)])
+def test_locate_inverts_the_causal_order(bh, n, rows):
     sc = Schedule(bh, n, rows, causal=True)
+    assert sorted(sc.order()) == list(range(sc.q_blocks))
+    assert all(sc.pos_of(sc.qb_at(k)) == k for k in range(sc.q_blocks))
     step = max(1, sc.total() // 5000)
     for s in list(range(0, sc.total(), step)) + [sc.total() - 1]:
         u, j = sc.locate(s)
         assert 0 <= j < sc.steps_of(u % sc.q_blocks)
         assert sc.unit_first(u) + j == s
+    # the order walks every unit of every head once
+    u, seen = 0, []
+    while u < sc.bh * sc.q_blocks:
+        seen.append(u)
+        u = sc.next_unit(u)
+    assert sorted(seen) == list(range(sc.bh * sc.q_blocks))
+
+
+def test_causal_order_balances_unit_counts():
+    # B1 H8 N8192 causal: every CTA gets one to three query blocks (ascending order: 1 to 8)
+    sc, ctas, split = plan(8, 8192, 256, 148, True)
+    units = [len(list(cursor_segments(sc, split, c, ctas))) for c in range(ctas)]
+    assert split and max(units) <= 3
 
 
 def test_headline_shape_uses_split_and_all_sms():
