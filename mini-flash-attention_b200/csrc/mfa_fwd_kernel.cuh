@@ -173,7 +173,7 @@ struct StepCursor {
     sc.locate<kCausal>(b, u, j0);
     j = j0;
     const long long len = e - b;
-    const int avail = sc.steps_of<kCausal>(u % sc.q_blocks) - j0;
+    const int avail = sc.steps_of<kCausal>(sc.qb_of(u)) - j0;
     j1 = len < avail ? j0 + static_cast<int>(len) : j0 + avail;
     rem = static_cast<int>(len - (j1 - j0));
   }
@@ -181,7 +181,7 @@ struct StepCursor {
   __device__ bool first_step() const { return j == j0; }
   __device__ bool first_of_range() const { return seg_idx == 0; }
   __device__ bool whole(const Schedule& sc) const {
-    return j0 == 0 && j1 == sc.steps_of<kCausal>(u % sc.q_blocks);
+    return j0 == 0 && j1 == sc.steps_of<kCausal>(sc.qb_of(u));
   }
   // Advance to the next segment (the softmax warps walk a segment with their own counter).
   __device__ void next_segment(const FwdParams& p) {
@@ -192,7 +192,7 @@ struct StepCursor {
     if (++j >= j1 && rem > 0) {
       if (p.split) {
         u = p.sc.next_unit<kCausal>(u);
-        const int steps = p.sc.steps_of<kCausal>(u % p.sc.q_blocks);
+        const int steps = p.sc.steps_of<kCausal>(p.sc.qb_of(u));
         j1 = rem < steps ? rem : steps;
         rem -= j1;
       } else {
@@ -208,7 +208,7 @@ struct StepCursor {
 
 // Head and batch index of unit u: its (batch * head) row is u / q_blocks, heads fastest.
 __device__ __forceinline__ HeadBatch head_batch(const FwdParams& p, int u) {
-  const int bh = u / p.sc.q_blocks;
+  const int bh = p.sc.head_of(u);
   return {bh % p.heads, bh / p.heads};
 }
 
@@ -244,7 +244,7 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
         for (int x = 0; x < Cfg::kBoxes; ++x) {
           tma_load_4d(sbase + Cfg::kQOff + (b * Cfg::NQ + i) * Cfg::kTileBytes + x * Cfg::kBoxBytes,
                       &p.tm_q, bar(Cfg::kBarQFull + b), x * Cfg::kBoxCols,
-                      (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + i * Cfg::kRows, hb.h, hb.b);
+                      p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + i * Cfg::kRows, hb.h, hb.b);
         }
       }
       q_loaded = s + 1;
@@ -583,7 +583,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     float m_run[2] = {-INFINITY, -INFINITY};  // running max of s*scale*log2(e), per row
     float l_run[2] = {0.0f, 0.0f};            // this thread's partial row sums
     const int row0 =  // first query row of this warp's slice (causal masking only)
-        Cfg::kCausal ? (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows + slice : 0;
+        Cfg::kCausal ? p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows + slice : 0;
     for (int j = cur.j0; j < cur.j1; ++j, ++g) {
       if (!softmax_step<Cfg>(p, bars, tS, tP, tO, tile, lane, g, j, row0, j == cur.j0, m_run,
                              l_run, wd))
@@ -609,10 +609,10 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
         // log-sum-exp = ln 2 * (m + log2 l), m in scaled log2 units
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-          const int qrow = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows +
+          const int qrow = p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows +
                            slice + gq + 8 * r;
           if (qrow < p.n)
-            p.lse[static_cast<size_t>(cur.u / p.sc.q_blocks) * p.n + qrow] =
+            p.lse[static_cast<size_t>(p.sc.head_of(cur.u)) * p.n + qrow] =
                 (m_run[r] + log2f(l_row[r])) * 0.6931471805599453f;
         }
       }
@@ -645,7 +645,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
           if (!wait_single(bar(Cfg::kBarStage + tile), static_cast<uint32_t>(stores) & 1u, wd,
                            kSiteSoftStage))
             return;
-          const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
+          const int r0 = p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
           if (r0 < p.n) {
             const HeadBatch ob = head_batch(p, cur.u);
 #pragma unroll
@@ -708,7 +708,7 @@ __device__ __forceinline__ void store_role(const FwdParams& p, uint8_t* smem, ui
           ok = false;
           break;
         }
-        const int r0 = (cur.u % p.sc.q_blocks) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
+        const int r0 = p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
         if (r0 < p.n) {
           const uint32_t stage =
               smem_addr(smem + Cfg::kQOff + (b * Cfg::NQ + tile) * Cfg::kTileBytes);
@@ -836,7 +836,7 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   int u = 0, j = 0;
   if (b1 > b0) mp.sc.locate<kCausal>(b1 - 1, u, j);  // query block holding c's last step
   const long long u0 = mp.sc.unit_first<kCausal>(u);
-  const long long u1 = u0 + mp.sc.steps_of<kCausal>(u % mp.sc.q_blocks);
+  const long long u1 = u0 + mp.sc.steps_of<kCausal>(mp.sc.qb_of(u));
   // Merged here only if it starts inside c and ends past it.
   if (!(b1 > b0 && u1 > b1 && u0 >= b0)) {
     grid_dependency_wait();
@@ -853,8 +853,8 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   }
   const int r = static_cast<int>(threadIdx.x) / kMergeThreadsPerRow;
   const int k = static_cast<int>(threadIdx.x) % kMergeThreadsPerRow;
-  const int bh = u / mp.sc.q_blocks;
-  const int qrow = (u % mp.sc.q_blocks) * kRowsPerUnit + r;
+  const int bh = mp.sc.head_of(u);
+  const int qrow = (u - bh * mp.sc.q_blocks) * kRowsPerUnit + r;
   const long long offset = static_cast<long long>(bh / mp.heads) * mp.stride_b +
                            static_cast<long long>(bh % mp.heads) * mp.stride_h +
                            static_cast<long long>(qrow) * mp.stride_n;

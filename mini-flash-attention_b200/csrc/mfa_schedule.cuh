@@ -27,6 +27,17 @@ struct Schedule {
   int group;             // rows_per_unit / 128
   int causal;            // 1: query block qb stops at key block group * (qb + 1)
   long long head_steps;  // steps of one head
+  // u / q_blocks for 0 <= u < 2^31 as (u * qb_mul) >> qb_shift (set by make_schedule): the
+  // kernels split unit indices at every unit change, where a hardware-free division would
+  // cost ~20 instructions.
+  uint32_t qb_mul;
+  int qb_shift;
+
+  __host__ __device__ int head_of(int u) const {
+    const uint64_t prod = static_cast<uint64_t>(static_cast<uint32_t>(u)) * qb_mul;
+    return static_cast<int>(prod >> qb_shift);
+  }
+  __host__ __device__ int qb_of(int u) const { return u - head_of(u) * q_blocks; }
 
   // The kernels use the forms with the masking mode as a compile-time argument (kCausal must
   // equal `causal`), so that the non-causal kernels carry none of the causal arithmetic.
@@ -64,13 +75,13 @@ struct Schedule {
   // First global step of unit u.
   template <bool kCausal>
   __host__ __device__ long long unit_first(int u) const {
-    return static_cast<long long>(u / q_blocks) * head_steps + first_of<kCausal>(u % q_blocks);
+    return static_cast<long long>(head_of(u)) * head_steps + first_of<kCausal>(qb_of(u));
   }
   // The unit processed after unit u (in split mode, where a CTA walks consecutive steps).
   template <bool kCausal>
   __host__ __device__ int next_unit(int u) const {
     if (!kCausal) return u + 1;
-    const int head = u / q_blocks;
+    const int head = head_of(u);
     const int k = pos_of(u - head * q_blocks) + 1;
     return k < q_blocks ? head * q_blocks + qb_at(k) : (head + 1) * q_blocks;
   }
@@ -119,6 +130,15 @@ inline Schedule make_schedule(long long bh, long long n, int rows_per_unit, int 
   s.q_blocks = static_cast<int>((n + rows_per_unit - 1) / rows_per_unit);
   s.nkb = static_cast<int>((n + keys_per_block - 1) / keys_per_block);
   s.group = rows_per_unit / keys_per_block;
+  // magic division by q_blocks (d): shift = 31 + ceil(log2 d), mul = ceil(2^shift / d) < 2^32;
+  // the error of u * mul / 2^shift stays below 2^-ceil(log2 d) <= 1/d for u < 2^31
+  {
+    const uint64_t d = static_cast<uint64_t>(s.q_blocks);
+    int lg = 0;
+    while ((uint64_t{1} << lg) < d) ++lg;
+    s.qb_shift = 31 + lg;
+    s.qb_mul = static_cast<uint32_t>(((uint64_t{1} << s.qb_shift) + d - 1) / d);
+  }
   s.causal = causal ? 1 : 0;
   s.head_steps = causal ? s.pos_first(s.q_blocks - 1) + s.steps_of<true>(s.qb_at(s.q_blocks - 1))
                        : s.first_of<false>(s.q_blocks - 1) + s.steps_of<false>(s.q_blocks - 1);

@@ -272,3 +272,26 @@ def test_causal_halves_the_work():
     # 32 query blocks: 2 + 4 + ... + 64 key blocks
     assert sc.total() == 2 * 32 * 33 // 2
     assert abs(sc.total() / full.total() - 0.5) < 0.02
+
+
+def magic(d):
+    """Multiplier and shift of Schedule::head_of (make_schedule in csrc/mfa_schedule.cuh)."""
+    lg = 0
+    while (1 << lg) < d:
+        lg += 1
+    shift = 31 + lg
+    return -(-(1 << shift) // d), shift
+
+
+@pytest.mark.parametrize("d", [1, 2, 3, 5, 7, 31, 32, 33, 64, 100, 127, 129, 4095, 65537,
+                               (1 << 20) + 1, (1 << 30) + 3, (1 << 31) - 1])
+def test_magic_division_by_query_blocks(d):
+    import random
+    mul, shift = magic(d)
+    assert mul < 1 << 32
+    rng = random.Random(d)
+    us = [0, 1, d - 1, d, d + 1, (1 << 31) - 1, (1 << 31) - 2] + \
+        [rng.randrange(1 << 31) for _ in range(2000)] + [d * k - 1 for k in range(1, 50)]
+    for u in us:
+        if 0 <= u < 1 << 31:
+            assert (u * mul) >> shift == u // d, (u, d)
