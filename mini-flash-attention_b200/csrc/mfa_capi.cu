@@ -261,6 +261,7 @@ int plan_forward(int64_t bh, int64_t n, int64_t sms, Plan& pl) {
     if (busy < 0.97) pl.split = 1;
   }
   if (pl.split) pl.ctas = total < sms ? total : sms;
+  set_ctas(pl.sc, static_cast<int>(pl.ctas));
   // every CTA's work must stay below 2^31 steps (32-bit step counters in the kernel)
   if ((pl.split ? total / pl.ctas + 1 : (units + pl.ctas - 1) / pl.ctas * nkb) >= 0x7fffffffLL)
     return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");

@@ -165,7 +165,7 @@ struct StepCursor {
       return;
     }
     long long b, e;
-    split_range(sc.total(), static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x), b, e);
+    sc.range(static_cast<int>(blockIdx.x), b, e);  // gridDim.x == sc.ctas
     if (b >= e) {
       u = j = j0 = j1 = rem = 0;
       return;
@@ -747,50 +747,59 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
   // The split-mode merge kernel may be scheduled now; it waits for this grid to complete
   // before reading anything this grid writes.
   if (threadIdx.x == 0) grid_dependents_launch();
-  if (threadIdx.x == 0) {
-    *abort_flag = 0;
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bars + 8 * (Cfg::kBarQFull + b), 1);
-      mbar_init(bars + 8 * (Cfg::kBarQEmpty + b), Cfg::NQ);  // one arrive per tile epilogue
+  // The load thread initialises the barriers and goes straight on to its first copies; the
+  // other warps wait on named barrier 1 for the barriers and for warp 0's TMEM allocation
+  // (the load warp only arrives there), so the first Q/K/V loads leave while TMEM is set up.
+  uint32_t tmem = 0;  // TMEM base (all warps but the load warp)
+  if (warp == Cfg::kLoadWarp) {
+    if (lane == 0) {
+      *abort_flag = 0;
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(bars + 8 * (Cfg::kBarQFull + b), 1);
+        mbar_init(bars + 8 * (Cfg::kBarQEmpty + b), Cfg::NQ);  // one arrive per tile epilogue
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_init(bars + 8 * (Cfg::kBarKFull + s), 1);
+        mbar_init(bars + 8 * (Cfg::kBarKEmpty + s), 1);
+        mbar_init(bars + 8 * (Cfg::kBarVFull + s), 1);
+        mbar_init(bars + 8 * (Cfg::kBarVEmpty + s), 1);
+      }
+      for (int i = 0; i < NQ; ++i) {
+        mbar_init(bars + 8 * (Cfg::kBarSFull + i), 1);
+        mbar_init(bars + 8 * (Cfg::kBarSFree + i), 8);  // one arrive per softmax warp of tile i
+        mbar_init(bars + 8 * (Cfg::kBarPFull + i), 8);
+        mbar_init(bars + 8 * (Cfg::kBarODone + i), 1);
+      }
+      for (int i = 0; i < NQ; ++i) mbar_init(bars + 8 * (Cfg::kBarStage + i), 8);
+      mbar_init(bars + 8 * Cfg::kBarDrain, 1);
+      mbar_init_fence();
     }
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bars + 8 * (Cfg::kBarKFull + s), 1);
-      mbar_init(bars + 8 * (Cfg::kBarKEmpty + s), 1);
-      mbar_init(bars + 8 * (Cfg::kBarVFull + s), 1);
-      mbar_init(bars + 8 * (Cfg::kBarVEmpty + s), 1);
-    }
-    for (int i = 0; i < NQ; ++i) {
-      mbar_init(bars + 8 * (Cfg::kBarSFull + i), 1);
-      mbar_init(bars + 8 * (Cfg::kBarSFree + i), 8);  // one arrive per softmax warp of tile i
-      mbar_init(bars + 8 * (Cfg::kBarPFull + i), 8);
-      mbar_init(bars + 8 * (Cfg::kBarODone + i), 1);
-    }
-    for (int i = 0; i < NQ; ++i) mbar_init(bars + 8 * (Cfg::kBarStage + i), 8);
-    mbar_init(bars + 8 * Cfg::kBarDrain, 1);
-    mbar_init_fence();
-  }
-  if (warp == 0) {
-    tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const Watchdog wd{abort_flag, p.status, p.timeout_ns};
-
-  if (warp >= Cfg::kSoftmaxWarps) {
+    __syncwarp();
+    named_bar_arrive(1, Cfg::kThreads);
     if constexpr (Cfg::kRebalanceRegs) setmaxnreg_dec<Cfg::kControlRegs>();
-    if (warp == Cfg::kLoadWarp) {
-      if (lane == 0) load_role<Cfg>(p, smem, bars, wd);
-    } else if (warp == Cfg::kMmaWarp) {
-      mma_role<Cfg>(p, smem, bars, tmem, wd);
-    } else if (Cfg::kStoreRole && warp == Cfg::kStoreWarp) {
-      if (lane == 0) store_role<Cfg>(p, smem, bars, wd);
-    }
+    const Watchdog wd{abort_flag, p.status, p.timeout_ns};
+    if (lane == 0) load_role<Cfg>(p, smem, bars, wd);
   } else {
-    if constexpr (Cfg::kRebalanceRegs) setmaxnreg_inc<Cfg::kSoftmaxRegs>();
-    softmax_role<Cfg>(p, smem, bars, tmem, warp / 8, wd);
+    if (warp == 0) {
+      tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    named_bar_sync(1, Cfg::kThreads);
+    tc_fence_after();
+    tmem = *tmem_slot;
+    const Watchdog wd{abort_flag, p.status, p.timeout_ns};
+    if (warp < Cfg::kSoftmaxWarps) {
+      if constexpr (Cfg::kRebalanceRegs) setmaxnreg_inc<Cfg::kSoftmaxRegs>();
+      softmax_role<Cfg>(p, smem, bars, tmem, warp / 8, wd);
+    } else {
+      if constexpr (Cfg::kRebalanceRegs) setmaxnreg_dec<Cfg::kControlRegs>();
+      if (warp == Cfg::kMmaWarp) {
+        mma_role<Cfg>(p, smem, bars, tmem, wd);
+      } else if (Cfg::kStoreRole && warp == Cfg::kStoreWarp) {
+        if (lane == 0) store_role<Cfg>(p, smem, bars, wd);
+      }
+    }
   }
   __syncwarp();
   tc_fence_before();
@@ -830,9 +839,8 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   constexpr int kOffL = kRowsPerUnit * (kD + 1);         // row sums within a slot
   constexpr int kBatch = kChunks <= 4 ? 2 : 1;           // pieces read per round trip
   const int c = static_cast<int>(blockIdx.x);
-  const long long total = mp.sc.total();
   long long b0, b1;
-  split_range(total, c, mp.ctas, b0, b1);
+  mp.sc.range(c, b0, b1);
   int u = 0, j = 0;
   if (b1 > b0) mp.sc.locate<kCausal>(b1 - 1, u, j);  // query block holding c's last step
   const long long u0 = mp.sc.unit_first<kCausal>(u);
@@ -847,7 +855,7 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
   int pieces = 1;
   for (int cc = c + 1; cc < mp.ctas; ++cc) {
     long long s0, s1;
-    split_range(total, cc, mp.ctas, s0, s1);
+    mp.sc.range(cc, s0, s1);
     if (s0 >= u1) break;
     ++pieces;
   }

@@ -20,6 +20,25 @@
 
 namespace mfa {
 
+// n / d for 0 <= n < 2^31 as (n * mul) >> shift: shift = 31 + ceil(log2 d) and
+// mul = ceil(2^shift / d) < 2^32, so the error of n * mul / 2^shift stays below
+// 2^-ceil(log2 d) <= 1/d. The kernels split step and unit indices with it where a division
+// by a runtime value would cost ~20 (32-bit) or ~100 (64-bit) instructions.
+struct Div31 {
+  uint32_t mul;
+  int shift;
+  void set(long long d) {
+    int lg = 0;
+    while ((1LL << lg) < d) ++lg;
+    shift = 31 + lg;
+    mul = static_cast<uint32_t>(((uint64_t{1} << shift) + static_cast<uint64_t>(d) - 1) /
+                                static_cast<uint64_t>(d));
+  }
+  __host__ __device__ uint32_t operator()(uint32_t n) const {
+    return static_cast<uint32_t>((static_cast<uint64_t>(n) * mul) >> shift);
+  }
+};
+
 struct Schedule {
   int bh;                // batch * heads
   int q_blocks;          // query blocks per head: ceil(N / rows_per_unit)
@@ -27,17 +46,30 @@ struct Schedule {
   int group;             // rows_per_unit / 128
   int causal;            // 1: query block qb stops at key block group * (qb + 1)
   long long head_steps;  // steps of one head
-  // u / q_blocks for 0 <= u < 2^31 as (u * qb_mul) >> qb_shift (set by make_schedule): the
-  // kernels split unit indices at every unit change, where a hardware-free division would
-  // cost ~20 instructions.
-  uint32_t qb_mul;
-  int qb_shift;
+  // split mode: CTA c of `ctas` takes the global steps [c * total / ctas, (c+1) * total / ctas),
+  // computed as c * cta_q + c * cta_r / ctas with total = cta_q * ctas + cta_r (set_ctas)
+  int ctas;
+  int cta_r;
+  long long cta_q;
+  Div31 qdiv;  // by q_blocks (unit -> head)
+  Div31 kdiv;  // by nkb (step -> unit, non-causal), for steps < 2^31
+  Div31 hdiv;  // by head_steps (step -> head, causal), if head_steps < 2^31
+  Div31 pdiv;  // by pair_steps() (causal locate within a head)
 
-  __host__ __device__ int head_of(int u) const {
-    const uint64_t prod = static_cast<uint64_t>(static_cast<uint32_t>(u)) * qb_mul;
-    return static_cast<int>(prod >> qb_shift);
-  }
+  __host__ __device__ int head_of(int u) const { return static_cast<int>(qdiv(u)); }
   __host__ __device__ int qb_of(int u) const { return u - head_of(u) * q_blocks; }
+
+  // Steps [begin, end) of CTA `cta` in split mode.
+  __host__ __device__ void range(int cta, long long& begin, long long& end) const {
+    // cta_r * cta < ctas^2 < 2^32 (ctas <= 65535, checked by set_ctas)
+    const auto part = [&](int c) {
+      return cta_q * c + static_cast<long long>(static_cast<uint32_t>(cta_r) *
+                                                static_cast<uint32_t>(c) /
+                                                static_cast<uint32_t>(ctas));
+    };
+    begin = part(cta);
+    end = part(cta + 1);
+  }
 
   // The kernels use the forms with the masking mode as a compile-time argument (kCausal must
   // equal `causal`), so that the non-causal kernels carry none of the causal arithmetic.
@@ -88,13 +120,16 @@ struct Schedule {
   // Unit u and key block j of global step s (0 <= s < total()).
   template <bool kCausal>
   __host__ __device__ void locate(long long s, int& u, int& j) const {
+    const bool small = s < (1LL << 31);
     if (!kCausal) {  // every query block has nkb steps
-      const long long uu = s / nkb;
+      const long long uu = small ? static_cast<long long>(kdiv(static_cast<uint32_t>(s))) : s / nkb;
       u = static_cast<int>(uu);
       j = static_cast<int>(s - uu * nkb);
       return;
     }
-    const long long head = s / head_steps;
+    const long long head = small && head_steps < (1LL << 31)
+                               ? static_cast<long long>(hdiv(static_cast<uint32_t>(s)))
+                               : s / head_steps;
     const long long r = s - head * head_steps;
     const int pairs = q_blocks >> 1;
     int k;
@@ -103,8 +138,10 @@ struct Schedule {
       k = 0;
       rem = r;
     } else if (pairs > 1 && r < pair0() + (pairs - 1) * pair_steps()) {
-      const long long t = r - pair0();
-      const long long m = 1 + t / pair_steps();
+      const long long t = r - pair0();  // < head_steps; pair_steps() < 2^31 (see set_ctas)
+      const long long m =
+          1 + (t < (1LL << 31) ? static_cast<long long>(pdiv(static_cast<uint32_t>(t)))
+                               : t / pair_steps());
       k = static_cast<int>(2 * m);
       rem = t - (m - 1) * pair_steps();
     } else {  // the middle query block of an odd count, alone at the last position
@@ -130,26 +167,24 @@ inline Schedule make_schedule(long long bh, long long n, int rows_per_unit, int 
   s.q_blocks = static_cast<int>((n + rows_per_unit - 1) / rows_per_unit);
   s.nkb = static_cast<int>((n + keys_per_block - 1) / keys_per_block);
   s.group = rows_per_unit / keys_per_block;
-  // magic division by q_blocks (d): shift = 31 + ceil(log2 d), mul = ceil(2^shift / d) < 2^32;
-  // the error of u * mul / 2^shift stays below 2^-ceil(log2 d) <= 1/d for u < 2^31
-  {
-    const uint64_t d = static_cast<uint64_t>(s.q_blocks);
-    int lg = 0;
-    while ((uint64_t{1} << lg) < d) ++lg;
-    s.qb_shift = 31 + lg;
-    s.qb_mul = static_cast<uint32_t>(((uint64_t{1} << s.qb_shift) + d - 1) / d);
-  }
   s.causal = causal ? 1 : 0;
   s.head_steps = causal ? s.pos_first(s.q_blocks - 1) + s.steps_of<true>(s.qb_at(s.q_blocks - 1))
                        : s.first_of<false>(s.q_blocks - 1) + s.steps_of<false>(s.q_blocks - 1);
+  s.qdiv.set(s.q_blocks);
+  s.kdiv.set(s.nkb);
+  s.hdiv.set(s.head_steps < (1LL << 31) ? s.head_steps : 1);
+  s.pdiv.set(s.pair_steps());
+  s.ctas = 1;
+  s.cta_q = s.total();
+  s.cta_r = 0;
   return s;
 }
 
-// Split-mode range of CTA `cta` of `ctas` over the global steps: [begin, end).
-__host__ __device__ inline void split_range(long long total, int cta, int ctas, long long& begin,
-                                            long long& end) {
-  begin = total * cta / ctas;
-  end = total * (cta + 1) / ctas;
+// Split mode over `ctas` CTAs (1 <= ctas <= 65535).
+inline void set_ctas(Schedule& s, int ctas) {
+  s.ctas = ctas;
+  s.cta_q = s.total() / ctas;
+  s.cta_r = static_cast<int>(s.total() % ctas);
 }
 
 }  // namespace mfa
