@@ -15,9 +15,13 @@
 //              dV += P^T dO and dK += dS^T q.
 // TMEM (columns): S or S^T [0,128), dP or dP^T [128,256), P^T / dS [256,320), dS^T [320,384),
 // accumulators dQ [320,384) or dV [384,448) and dK [448,512).
-// Warp roles as in the forward kernel (csrc/mfa_fwd_kernel.cuh): 8 softmax-side warps on
+// Warp roles as in the forward kernel (csrc/mfa_fwd_kernel.cuh): 16 softmax-side warps on
 // 16x256b TMEM fragments (lane 4g + q: rows g and g + 8 of a 16-row slice, columns 2q, 2q + 1
 // of every 8), one MMA warp (one elected lane issues), one TMA warp; every wait is bounded.
+// The backward needs no row reductions (L and D come precomputed), so the 128 columns of a
+// block are split between two warps per 16-row slice: warp w takes TMEM lane quadrant w % 4,
+// slice half (w / 4) % 2 and column half w / 8, which doubles the warps that hide each other's
+// latencies at the same TMEM footprint.
 #pragma once
 
 #include <cuda.h>
@@ -57,10 +61,16 @@ struct BwdConfig {
   static constexpr int kCols = 128;  // streamed rows per step
   static constexpr int kTileBytes = kRows * kHeadDim * 2;
   static constexpr int STAGES = 3;
-  static constexpr int kSoftmaxWarps = 8;
-  static constexpr int kMmaWarp = 8;
-  static constexpr int kLoadWarp = 9;
-  static constexpr int kThreads = 320;
+  static constexpr int kSoftmaxWarps = 16;  // 16 rows x 64 columns each
+  static constexpr int kMmaWarp = 16;
+  static constexpr int kLoadWarp = 17;
+  // As in the forward kernel: 640 threads (the MMA and TMA warps fill a fifth warpgroup, 2
+  // warps idle) launch with 96 registers; setmaxnreg moves the control warpgroup to 64 and
+  // the four softmax-side warpgroups to 104 (512 x 104 + 128 x 64 = 640 x 96; per SM
+  // sub-partition 4 x 104 + 64 <= 512 registers per lane).
+  static constexpr int kThreads = 32 * 20;
+  static constexpr int kSoftmaxRegs = 104;
+  static constexpr int kControlRegs = 64;
 
   // shared memory (1024-aligned base)
   static constexpr int kResOff = 0;                                  // [2 buffers][x, y]
@@ -73,10 +83,10 @@ struct BwdConfig {
   static constexpr int kBarStrFull = 4;   // [STAGES]
   static constexpr int kBarStrEmpty = kBarStrFull + STAGES;
   static constexpr int kBarSSFull = kBarStrEmpty + STAGES;  // S and dP computed
-  static constexpr int kBarSSFree = kBarSSFull + 1;         // S and dP read by all 8 warps
-  static constexpr int kBarOpFull = kBarSSFree + 1;         // fp16 operands written (8 warps)
+  static constexpr int kBarSSFree = kBarSSFull + 1;         // S and dP read by all 16 warps
+  static constexpr int kBarOpFull = kBarSSFree + 1;         // fp16 operands written (16 warps)
   static constexpr int kBarAccDone = kBarOpFull + 1;        // TS MMAs of a step completed
-  static constexpr int kBarStage = kBarAccDone + 1;         // output staging written (8 warps)
+  static constexpr int kBarStage = kBarAccDone + 1;         // output staging written (16 warps)
   static constexpr int kBarDrain = kBarStage + 1;
   static constexpr int kNumBars = kBarDrain + 1;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
@@ -312,7 +322,7 @@ unwind:
 template <class Cfg>
 __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint32_t bars,
                                          uint32_t tS, uint32_t tDP, uint32_t tOp0, uint32_t tOp1,
-                                         int lane, int g, int blk, int j, int row0,
+                                         int lane, int half, int g, int blk, int j, int row0,
                                          const float (&lrow)[2], const float (&drow)[2],
                                          const Watchdog& wd) {
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
@@ -320,14 +330,16 @@ __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint
   if (!wait_warp(bar(Cfg::kBarSSFull), static_cast<uint32_t>(g) & 1u, wd, kSiteSoftSFull))
     return false;
   tc_fence_after();
-  uint32_t sr[64], dp[64];  // [4i + e]: row g + 8 (e / 2), column 8i + 2q + e % 2
+  // [4i + e]: row g + 8 (e / 2), column 64 * half + 8i + 2q + e % 2 (tS, tDP already point at
+  // this warp's column half)
+  uint32_t sr[32], dp[32];
   tmem_ld_16x256b_sync(tS, sr);
   tmem_ld_16x256b_sync(tDP, dp);
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(bar(Cfg::kBarSSFree));
 
-  const int q2 = 2 * (lane & 3);
+  const int q2 = 2 * (lane & 3) + 64 * half;  // first of this thread's columns in a block
   const int gq = lane >> 2;
   if (!Cfg::kDKV) {
     // keys past N (last key block) and, with the mask, keys after the query row
@@ -335,7 +347,7 @@ __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint
       const int valid = p.n - j * Cfg::kCols;
       if (valid < Cfg::kCols) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             if (8 * i + q2 + (e & 1) >= valid) sr[4 * i + e] = __float_as_uint(-INFINITY);
@@ -345,7 +357,7 @@ __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint
       const int t0 = row0 + gq - j * Cfg::kCols;  // column k masked when k > t0 (+8 for e >= 2)
       if (j * Cfg::kCols + Cfg::kCols - 1 > row0) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             if (8 * i + q2 + (e & 1) > t0 + 8 * (e >> 1)) sr[4 * i + e] = __float_as_uint(-INFINITY);
@@ -355,14 +367,14 @@ __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint
     // diagonal block: queries (columns) before the key row score -inf
     const int t0 = row0 + gq - j * Cfg::kCols;  // column k masked when k < t0 (+8 for e >= 2)
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         if (8 * i + q2 + (e & 1) < t0 + 8 * (e >> 1)) sr[4 * i + e] = __float_as_uint(-INFINITY);
   }
 
   const uint64_t c2 = f2_splat(p.scale_log2);
-  uint32_t pk[32], dk[32];  // [2i + r]: row g + 8r, columns 8i + 2q, 8i + 2q + 1 (16x128b)
+  uint32_t pk[16], dk[16];  // [2i + r]: row g + 8r, columns 8i + q2, 8i + q2 + 1 (16x128b)
   const int st = g % Cfg::STAGES;
   const float* vec = reinterpret_cast<const float*>(smem + Cfg::kVecOff + st * Cfg::kVecBytes);
   if (Cfg::kDKV) {
@@ -373,7 +385,7 @@ __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint
       return false;
   }
 #pragma unroll
-  for (int k = 0; k < 32; ++k) {
+  for (int k = 0; k < 16; ++k) {
     const int i = k >> 1, r = k & 1;
     uint64_t nl, d2;
     if (Cfg::kDKV) {
@@ -403,10 +415,10 @@ __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint
     tc_fence_after();
   }
   if (Cfg::kDKV) {
-    tmem_st_16x128b_x16(tOp0, pk);
-    tmem_st_16x128b_x16(tOp1, dk);
+    tmem_st_16x128b_x8(tOp0, pk);
+    tmem_st_16x128b_x8(tOp1, dk);
   } else {
-    tmem_st_16x128b_x16(tOp0, dk);
+    tmem_st_16x128b_x8(tOp0, dk);
   }
   tmem_wait_st();
   tc_fence_before();
@@ -422,11 +434,15 @@ __device__ __forceinline__ void bwd_softmax_role(const BwdParams& p, uint8_t* sm
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int slice = (warp & 3) * 32 + ((warp >> 2) & 1) * 16;
+  const int half = warp >> 3;  // columns [64 half, 64 half + 64) of a block
   const int gq = lane >> 2;
   const int q = lane & 3;
   const uint32_t lb = static_cast<uint32_t>(slice) << 16;
-  const uint32_t tS = tmem + lb + Cfg::kColS, tDP = tmem + lb + Cfg::kColDP;
-  const uint32_t tOp0 = tmem + lb + Cfg::kColOp0, tOp1 = tmem + lb + Cfg::kColOp1;
+  const uint32_t tS = tmem + lb + Cfg::kColS + 64 * half;
+  const uint32_t tDP = tmem + lb + Cfg::kColDP + 64 * half;
+  // P / dS operands: fp16 / bf16 pairs, 32 columns per half
+  const uint32_t tOp0 = tmem + lb + Cfg::kColOp0 + 32 * half;
+  const uint32_t tOp1 = tmem + lb + Cfg::kColOp1 + 32 * half;
   const bool leader = warp == 0 && lane == 0;
 
   int g = 0, stores = 0;
@@ -447,8 +463,8 @@ __device__ __forceinline__ void bwd_softmax_role(const BwdParams& p, uint8_t* sm
     }
     const int j0 = cur.j0, j1 = cur.j1, b = cur.seg & 1;
     for (int j = j0; j < j1; ++j, ++g) {
-      if (!bwd_step<Cfg>(p, smem, bars, tS, tDP, tOp0, tOp1, lane, g, blk, j, row0, lrow, drow,
-                         wd))
+      if (!bwd_step<Cfg>(p, smem, bars, tS, tDP, tOp0, tOp1, lane, half, g, blk, j, row0, lrow,
+                         drow, wd))
         return;
     }
     // ---- unit epilogue: accumulators -> (scaled) fp16 / bf16 -> staging -> TMA
@@ -456,17 +472,21 @@ __device__ __forceinline__ void bwd_softmax_role(const BwdParams& p, uint8_t* sm
       return;
     tc_fence_after();
     uint8_t* res = smem + Cfg::kResOff + b * 2 * Cfg::kTileBytes;
+    // this warp's 32 of the 64 accumulator columns (its column half), 16-byte chunks
+    // 4 half .. 4 half + 3 of each of its rows in the 128B-swizzled staging tile
     auto stage_acc = [&](uint32_t col, float mul, uint8_t* dst_tile) {
-      uint32_t a[32];
-      tmem_ld_16x256b_sync(tmem + lb + col, a);
+      uint32_t a[16];
+      tmem_ld_16x256b_sync(tmem + lb + col + 32 * half, a);
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int row = slice + gq + 8 * r;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           const uint32_t w = pack_pair<Cfg::kBF16>(__uint_as_float(a[4 * i + 2 * r]) * mul,
                                                    __uint_as_float(a[4 * i + 2 * r + 1]) * mul);
-          const uint32_t dst = smem_addr(dst_tile + row * 128 + ((i ^ (row & 7)) << 4) + 4 * q);
+          const int chunk = 4 * half + i;
+          const uint32_t dst =
+              smem_addr(dst_tile + row * 128 + ((chunk ^ (row & 7)) << 4) + 4 * q);
           asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst), "r"(w) : "memory");
         }
       }
@@ -500,7 +520,8 @@ __device__ __forceinline__ void bwd_softmax_role(const BwdParams& p, uint8_t* sm
 }
 
 template <bool kDKV, bool kCausal, bool kBF16>
-__global__ void __launch_bounds__(320, 1) mfa_bwd_kernel(const __grid_constant__ BwdParams p) {
+__global__ void __launch_bounds__(BwdConfig<kDKV, kCausal, kBF16>::kThreads, 1)
+    mfa_bwd_kernel(const __grid_constant__ BwdParams p) {
   using Cfg = BwdConfig<kDKV, kCausal, kBF16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -537,12 +558,16 @@ __global__ void __launch_bounds__(320, 1) mfa_bwd_kernel(const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const Watchdog wd{abort_flag, p.status, p.timeout_ns};
-  if (warp == Cfg::kLoadWarp) {
-    if (lane == 0) bwd_load_role<Cfg>(p, smem, bars, wd);
-  } else if (warp == Cfg::kMmaWarp) {
-    bwd_mma_role<Cfg>(p, smem, bars, tmem, wd);
-  } else {
+  if (warp < Cfg::kSoftmaxWarps) {
+    setmaxnreg_inc<Cfg::kSoftmaxRegs>();
     bwd_softmax_role<Cfg>(p, smem, bars, tmem, wd);
+  } else {
+    setmaxnreg_dec<Cfg::kControlRegs>();
+    if (warp == Cfg::kLoadWarp) {
+      if (lane == 0) bwd_load_role<Cfg>(p, smem, bars, wd);
+    } else if (warp == Cfg::kMmaWarp) {
+      bwd_mma_role<Cfg>(p, smem, bars, tmem, wd);
+    }
   }
   __syncwarp();
   tc_fence_before();

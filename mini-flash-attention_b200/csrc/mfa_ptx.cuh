@@ -325,6 +325,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 // ---- 16-lane fragment shapes. A warp reaches 16 TMEM lanes (rows) from the lane in taddr;
 // thread t works on rows g = t/4 and g + 8 and on the columns selected by q = t%4.
 // 64 columns: r[2i + e] -> row g + 8e, column 4i + q (i < 16).
+// 16x128b.x8: 32 columns of fp16 / bf16 pairs (64 keys or queries of a P / dS tile).
+__device__ __forceinline__ void tmem_st_16x128b_x8(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x128b.x8.b32 [%0], {"
+      "%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16"
+      "};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_16x128b_x16(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.16x128b.x16.b32 [%0], {"
