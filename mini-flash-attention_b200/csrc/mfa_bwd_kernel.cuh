@@ -64,8 +64,9 @@ struct BwdConfig {
   static constexpr int kSoftmaxWarps = 16;  // 16 rows x 64 columns each
   static constexpr int kMmaWarp = 16;
   static constexpr int kLoadWarp = 17;
-  // As in the forward kernel: 640 threads (the MMA and TMA warps fill a fifth warpgroup, 2
-  // warps idle) launch with 96 registers; setmaxnreg moves the control warpgroup to 64 and
+  static constexpr int kStoreWarp = 18;  // TMA stores of finished units' gradients
+  // As in the forward kernel: 640 threads (the MMA, load and store warps fill a fifth
+  // warpgroup, 1 warp idle) launch with 96 registers; setmaxnreg moves the control warpgroup to 64 and
   // the four softmax-side warpgroups to 104 (512 x 104 + 128 x 64 = 640 x 96; per SM
   // sub-partition 4 x 104 + 64 <= 512 registers per lane).
   static constexpr int kThreads = 32 * 20;
@@ -443,9 +444,7 @@ __device__ __forceinline__ void bwd_softmax_role(const BwdParams& p, uint8_t* sm
   // P / dS operands: fp16 / bf16 pairs, 32 columns per half
   const uint32_t tOp0 = tmem + lb + Cfg::kColOp0 + 32 * half;
   const uint32_t tOp1 = tmem + lb + Cfg::kColOp1 + 32 * half;
-  const bool leader = warp == 0 && lane == 0;
-
-  int g = 0, stores = 0;
+  int g = 0;
   BwdCursor<Cfg> cur;
   cur.init(p);
   while (cur.valid()) {
@@ -500,23 +499,41 @@ __device__ __forceinline__ void bwd_softmax_role(const BwdParams& p, uint8_t* sm
     tc_fence_before();
     fence_proxy_async_smem();
     __syncwarp();
+    // staging rows written: the store warp takes the unit from here (bwd_store_role)
     if (lane == 0) mbar_arrive(bar(Cfg::kBarStage));
-    if (leader) {
-      if (!wait_single(bar(Cfg::kBarStage), static_cast<uint32_t>(stores) & 1u, wd,
-                       kSiteSoftStage))
-        return;
-      const int r0 = blk * Cfg::kRows;
-      const HeadBatch hb = bwd_head_batch(p, cur.u);
-      tma_store_4d(&p.tm_o0, smem_addr(res), 0, r0, hb.h, hb.b);
-      if (Cfg::kDKV) tma_store_4d(&p.tm_o1, smem_addr(res + Cfg::kTileBytes), 0, r0, hb.h, hb.b);
-      tma_store_commit();
-      tma_store_wait_read();
-      mbar_arrive(bar(Cfg::kBarResEmpty + b));
-    }
+    cur.j = cur.j1 - 1;
+    cur.step(p);
+  }
+}
+
+// One thread of the store warp: once the 16 softmax-side warps have staged a unit's gradients
+// in its resident buffers, store them with TMA and free the buffers for the load warp when
+// the stores have read them; the softmax-side warps go straight on to the next unit.
+template <class Cfg>
+__device__ __forceinline__ void bwd_store_role(const BwdParams& p, uint8_t* smem, uint32_t bars,
+                                               const Watchdog& wd) {
+  auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
+  BwdCursor<Cfg> cur;
+  cur.init(p);
+  int stores = 0;
+  while (cur.valid()) {
+    const int b = cur.seg & 1;
+    if (!wait_single(bar(Cfg::kBarStage), static_cast<uint32_t>(stores) & 1u, wd, kSiteSoftStage))
+      break;
+    uint8_t* res = smem + Cfg::kResOff + b * 2 * Cfg::kTileBytes;
+    const int r0 = (cur.u % p.blocks) * Cfg::kRows;
+    const HeadBatch hb = bwd_head_batch(p, cur.u);
+    tma_store_4d(&p.tm_o0, smem_addr(res), 0, r0, hb.h, hb.b);
+    if (Cfg::kDKV) tma_store_4d(&p.tm_o1, smem_addr(res + Cfg::kTileBytes), 0, r0, hb.h, hb.b);
+    tma_store_commit();
+    tma_store_wait_read();
+    mbar_arrive(bar(Cfg::kBarResEmpty + b));
     ++stores;
     cur.j = cur.j1 - 1;
     cur.step(p);
   }
+  // unwinding or done: shared memory must outlive every store's read of it
+  tma_store_wait_read();
 }
 
 template <bool kDKV, bool kCausal, bool kBF16>
@@ -531,42 +548,54 @@ __global__ void __launch_bounds__(BwdConfig<kDKV, kCausal, kBF16>::kThreads, 1)
   const uint32_t bars = smem_addr(smem + Cfg::kBarOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kTmemSlotOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kAbortOff);
-  if (threadIdx.x == 0) {
-    *abort_flag = 0;
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bars + 8 * (Cfg::kBarResFull + b), 1);
-      mbar_init(bars + 8 * (Cfg::kBarResEmpty + b), 1);
+  // As in the forward kernel: the load thread initialises the barriers and goes straight on
+  // to its first copies; the other warps wait on named barrier 1 for the barriers and warp
+  // 0's TMEM allocation (the load warp only arrives there).
+  uint32_t tmem = 0;
+  if (warp == Cfg::kLoadWarp) {
+    if (lane == 0) {
+      *abort_flag = 0;
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(bars + 8 * (Cfg::kBarResFull + b), 1);
+        mbar_init(bars + 8 * (Cfg::kBarResEmpty + b), 1);
+      }
+      for (int s = 0; s < Cfg::STAGES; ++s) {
+        mbar_init(bars + 8 * (Cfg::kBarStrFull + s), 1);
+        mbar_init(bars + 8 * (Cfg::kBarStrEmpty + s), 1);
+      }
+      mbar_init(bars + 8 * Cfg::kBarSSFull, 1);
+      mbar_init(bars + 8 * Cfg::kBarSSFree, Cfg::kSoftmaxWarps);
+      mbar_init(bars + 8 * Cfg::kBarOpFull, Cfg::kSoftmaxWarps);
+      mbar_init(bars + 8 * Cfg::kBarAccDone, 1);
+      mbar_init(bars + 8 * Cfg::kBarStage, Cfg::kSoftmaxWarps);
+      mbar_init(bars + 8 * Cfg::kBarDrain, 1);
+      mbar_init_fence();
     }
-    for (int s = 0; s < Cfg::STAGES; ++s) {
-      mbar_init(bars + 8 * (Cfg::kBarStrFull + s), 1);
-      mbar_init(bars + 8 * (Cfg::kBarStrEmpty + s), 1);
-    }
-    mbar_init(bars + 8 * Cfg::kBarSSFull, 1);
-    mbar_init(bars + 8 * Cfg::kBarSSFree, Cfg::kSoftmaxWarps);
-    mbar_init(bars + 8 * Cfg::kBarOpFull, Cfg::kSoftmaxWarps);
-    mbar_init(bars + 8 * Cfg::kBarAccDone, 1);
-    mbar_init(bars + 8 * Cfg::kBarStage, Cfg::kSoftmaxWarps);
-    mbar_init(bars + 8 * Cfg::kBarDrain, 1);
-    mbar_init_fence();
-  }
-  if (warp == 0) {
-    tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const Watchdog wd{abort_flag, p.status, p.timeout_ns};
-  if (warp < Cfg::kSoftmaxWarps) {
-    setmaxnreg_inc<Cfg::kSoftmaxRegs>();
-    bwd_softmax_role<Cfg>(p, smem, bars, tmem, wd);
-  } else {
+    __syncwarp();
+    named_bar_arrive(1, Cfg::kThreads);
     setmaxnreg_dec<Cfg::kControlRegs>();
-    if (warp == Cfg::kLoadWarp) {
-      if (lane == 0) bwd_load_role<Cfg>(p, smem, bars, wd);
-    } else if (warp == Cfg::kMmaWarp) {
-      bwd_mma_role<Cfg>(p, smem, bars, tmem, wd);
+    const Watchdog wd{abort_flag, p.status, p.timeout_ns};
+    if (lane == 0) bwd_load_role<Cfg>(p, smem, bars, wd);
+  } else {
+    if (warp == 0) {
+      tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    named_bar_sync(1, Cfg::kThreads);
+    tc_fence_after();
+    tmem = *tmem_slot;
+    const Watchdog wd{abort_flag, p.status, p.timeout_ns};
+    if (warp < Cfg::kSoftmaxWarps) {
+      setmaxnreg_inc<Cfg::kSoftmaxRegs>();
+      bwd_softmax_role<Cfg>(p, smem, bars, tmem, wd);
+    } else {
+      setmaxnreg_dec<Cfg::kControlRegs>();
+      if (warp == Cfg::kMmaWarp) {
+        bwd_mma_role<Cfg>(p, smem, bars, tmem, wd);
+      } else if (warp == Cfg::kStoreWarp) {
+        if (lane == 0) bwd_store_role<Cfg>(p, smem, bars, wd);
+      }
     }
   }
   __syncwarp();
