@@ -49,6 +49,10 @@ struct BwdParams {
   const float* di;           // [bh][blocks * 128]: rowsum(dO ⊙ o), 0 past N
   unsigned long long timeout_ns;
   int* status;
+  // CTAs [cta0, cta0 + ctas) of the launch run this pass
+  int cta0;
+  int ctas;
+  int by_length;  // causal only: deal units out by length (below), else strided
 };
 
 template <bool kDKV_, bool kCausal_, bool kBF16_>
@@ -104,9 +108,15 @@ struct BwdConfig {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-// Units are (batch * head, 128-row block) pairs, CTA c takes units c, c + gridDim.x, ... .
+// Units are (batch * head, 128-row block) pairs, u = bh * blocks + block.
 // dQ pass: unit = query block b, steps = key blocks [0, b + 1) with the causal mask, else all.
 // dK/dV pass: unit = key block b, steps = query blocks [b, blocks) with the mask, else all.
+// By default the pass's CTA c takes units c, c + ctas, ... (neighbouring CTAs on neighbouring
+// blocks of a head, so the streamed blocks come from L2). With the mask and few units per CTA
+// (by_length) unit lengths, which run from 1 to `blocks`, would leave CTAs unevenly loaded:
+// the units are then taken in order of decreasing length (i = 0, 1, ...: block b = blocks - 1
+// - i / bh for dQ, i / bh for dK/dV, head i % bh) and dealt out boustrophedon (wave k goes to
+// CTAs 0..ctas-1 for even k, back from ctas-1 for odd k), which evens out the step counts.
 template <class Cfg>
 struct BwdCursor {
   int u;       // unit
@@ -125,12 +135,28 @@ struct BwdCursor {
     }
     j = j0;
   }
+  // Unit of this CTA's k-th assignment, or -1 past the end.
+  __device__ static int unit_at(const BwdParams& p, int k) {
+    // units <= 2^31 - 2^16 (checked by the launcher), k * ctas <= units: 32-bit arithmetic
+    const int c = static_cast<int>(blockIdx.x) - p.cta0;
+    const int units = p.bh * p.blocks;
+    if (!Cfg::kCausal || !p.by_length) {
+      const int u = k * p.ctas + c;
+      return u < units ? u : -1;
+    }
+    const int i = k * p.ctas + ((k & 1) ? p.ctas - 1 - c : c);
+    if (i >= units) return -1;
+    const int wave = i / p.bh, head = i - wave * p.bh;
+    const int blk = Cfg::kDKV ? wave : p.blocks - 1 - wave;
+    return head * p.blocks + blk;
+  }
   __device__ void init(const BwdParams& p) {
-    u = static_cast<int>(blockIdx.x);
     seg = 0;
-    if (u < p.bh * p.blocks) {
+    u = unit_at(p, 0);
+    if (u >= 0) {
       bounds(p);
     } else {
+      u = 0;
       j = j0 = j1 = 0;
     }
   }
@@ -138,8 +164,9 @@ struct BwdCursor {
   __device__ bool first_step() const { return j == j0; }
   __device__ void step(const BwdParams& p) {
     if (++j >= j1) {
-      u += static_cast<int>(gridDim.x);
-      if (u < p.bh * p.blocks) {
+      const int next = unit_at(p, seg + 1);
+      if (next >= 0) {
+        u = next;
         bounds(p);
         ++seg;
       }
@@ -536,10 +563,9 @@ __device__ __forceinline__ void bwd_store_role(const BwdParams& p, uint8_t* smem
   tma_store_wait_read();
 }
 
-template <bool kDKV, bool kCausal, bool kBF16>
-__global__ void __launch_bounds__(BwdConfig<kDKV, kCausal, kBF16>::kThreads, 1)
-    mfa_bwd_kernel(const __grid_constant__ BwdParams p) {
-  using Cfg = BwdConfig<kDKV, kCausal, kBF16>;
+// One CTA of one pass.
+template <class Cfg>
+__device__ __forceinline__ void bwd_cta(const BwdParams& p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -603,6 +629,37 @@ __global__ void __launch_bounds__(BwdConfig<kDKV, kCausal, kBF16>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+}
+
+// Both passes in one launch, at the same time on separate SMs: CTAs [0, pkv.cta0) run the dQ
+// pass, the rest the dK/dV pass. Used when a pass has few units per SM (512 equal units of
+// one pass on 148 SMs ran 4 units on some SMs and 3 on others).
+template <bool kCausal, bool kBF16>
+__global__ void __launch_bounds__(BwdConfig<true, kCausal, kBF16>::kThreads, 1)
+    mfa_bwd_kernel(const __grid_constant__ BwdParams pq, const __grid_constant__ BwdParams pkv) {
+  static_assert(BwdConfig<false, kCausal, kBF16>::kThreads ==
+                    BwdConfig<true, kCausal, kBF16>::kThreads,
+                "both passes run in one launch");
+  if (static_cast<int>(blockIdx.x) < pkv.cta0)
+    bwd_cta<BwdConfig<false, kCausal, kBF16>>(pq);
+  else
+    bwd_cta<BwdConfig<true, kCausal, kBF16>>(pkv);
+}
+
+// One pass per launch (many units per SM), all CTAs on it; a kernel of its own, which measured
+// 2-5% faster than the two-pass kernel above run with all CTAs on one pass.
+template <bool kDKV, bool kCausal, bool kBF16>
+__global__ void __launch_bounds__(BwdConfig<kDKV, kCausal, kBF16>::kThreads, 1)
+    mfa_bwd_pass_kernel(const __grid_constant__ BwdParams p) {
+  bwd_cta<BwdConfig<kDKV, kCausal, kBF16>>(p);
+}
+
+// Dynamic shared memory of the two-pass launch.
+template <bool kCausal, bool kBF16>
+constexpr int bwd_smem_bytes() {
+  return BwdConfig<false, kCausal, kBF16>::kSmemBytes > BwdConfig<true, kCausal, kBF16>::kSmemBytes
+             ? BwdConfig<false, kCausal, kBF16>::kSmemBytes
+             : BwdConfig<true, kCausal, kBF16>::kSmemBytes;
 }
 
 // D_i = rowsum(dO ⊙ o) and L2_i = L_i * log2(e) for every row, into [bh][blocks * 128] arrays

@@ -46,22 +46,27 @@ cudaError_t set_smem_attribute() {
       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
 }
 
-template <bool kDKV, bool kCausal, bool kBF16>
+template <bool kCausal, bool kBF16>
 cudaError_t set_bwd_attribute() {
-  return cudaFuncSetAttribute(mfa_bwd_kernel<kDKV, kCausal, kBF16>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              BwdConfig<kDKV, kCausal, kBF16>::kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(mfa_bwd_kernel<kCausal, kBF16>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       bwd_smem_bytes<kCausal, kBF16>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(mfa_bwd_pass_kernel<false, kCausal, kBF16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             BwdConfig<false, kCausal, kBF16>::kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(mfa_bwd_pass_kernel<true, kCausal, kBF16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             BwdConfig<true, kCausal, kBF16>::kSmemBytes);
+  return e;
 }
 
 cudaError_t set_bwd_attributes() {
-  cudaError_t e = set_bwd_attribute<false, false, false>();
-  if (e == cudaSuccess) e = set_bwd_attribute<false, true, false>();
-  if (e == cudaSuccess) e = set_bwd_attribute<false, false, true>();
-  if (e == cudaSuccess) e = set_bwd_attribute<false, true, true>();
-  if (e == cudaSuccess) e = set_bwd_attribute<true, false, false>();
-  if (e == cudaSuccess) e = set_bwd_attribute<true, true, false>();
-  if (e == cudaSuccess) e = set_bwd_attribute<true, false, true>();
-  if (e == cudaSuccess) e = set_bwd_attribute<true, true, true>();
+  cudaError_t e = set_bwd_attribute<false, false>();
+  if (e == cudaSuccess) e = set_bwd_attribute<true, false>();
+  if (e == cudaSuccess) e = set_bwd_attribute<false, true>();
+  if (e == cudaSuccess) e = set_bwd_attribute<true, true>();
   return e;
 }
 
@@ -596,22 +601,19 @@ int fwd_general(const void* q, const void* k, const void* v, void* out, float* l
 }
 
 // ---------------------------------------------------------------- backward
-template <bool kDKV, bool kCausal, bool kBF16>
-cudaError_t launch_bwd_pass(BwdParams& bp, const void* x, const void* y, const void* s0,
-                            const void* s1, void* o0, void* o1, int64_t batch, int64_t heads,
-                            int64_t n, int layout, int64_t ctas, cudaStream_t stream, int* rc) {
-  *rc = MFA_OK;
-  if ((*rc = encode_tensor(&bp.tm_x, x, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
-      (*rc = encode_tensor(&bp.tm_y, y, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
-      (*rc = encode_tensor(&bp.tm_s0, s0, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
-      (*rc = encode_tensor(&bp.tm_s1, s1, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
-      (*rc = encode_tensor(&bp.tm_o0, o0, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
-      (*rc = encode_tensor(&bp.tm_o1, o1 ? o1 : o0, batch, heads, n, 64, layout, kBF16)) != MFA_OK)
-    return cudaSuccess;
-  using Cfg = BwdConfig<kDKV, kCausal, kBF16>;
-  mfa_bwd_kernel<kDKV, kCausal, kBF16>
-      <<<static_cast<unsigned>(ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(bp);
-  return cudaGetLastError();
+// Tensor maps of one pass: x, y resident, s0, s1 streamed, o0 (and o1) written.
+template <bool kBF16>
+int encode_bwd_pass(BwdParams& bp, const void* x, const void* y, const void* s0, const void* s1,
+                    void* o0, void* o1, int64_t batch, int64_t heads, int64_t n, int layout) {
+  int rc = MFA_OK;
+  if ((rc = encode_tensor(&bp.tm_x, x, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (rc = encode_tensor(&bp.tm_y, y, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (rc = encode_tensor(&bp.tm_s0, s0, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (rc = encode_tensor(&bp.tm_s1, s1, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (rc = encode_tensor(&bp.tm_o0, o0, batch, heads, n, 64, layout, kBF16)) != MFA_OK ||
+      (rc = encode_tensor(&bp.tm_o1, o1 ? o1 : o0, batch, heads, n, 64, layout, kBF16)) != MFA_OK)
+    return rc;
+  return MFA_OK;
 }
 
 template <bool kCausal, bool kBF16>
@@ -631,9 +633,8 @@ int launch_backward(const void* q, const void* k, const void* v, const void* out
   if ((rc = check_device_pointers(lse, lse, lse, lse, dev)) != MFA_OK) return rc;
   const int64_t blocks = (n + 127) / 128;
   const int64_t units = bh * blocks;
-  if (units > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
+  if (units > 0x7fff0000LL) return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
   const int64_t sms = g_devices[dev].num_sms;
-  const int64_t ctas = units < sms ? units : sms;
   // L2 and D per row, padded to whole 128-row blocks per head
   const size_t rows = static_cast<size_t>(units) * 128;
   float* ws = nullptr;
@@ -661,12 +662,66 @@ int launch_backward(const void* q, const void* k, const void* v, const void* out
   bp.di = di;
   bp.timeout_ns = g_watchdog_ns;
   bp.status = g_devices[dev].status_ptr;
-  if (e == cudaSuccess && rc == MFA_OK)  // dQ: q, dO resident; k, v streamed
-    e = launch_bwd_pass<false, kCausal, kBF16>(bp, q, dout, k, v, dq, nullptr, batch, heads, n,
-                                               layout, ctas, stream, &rc);
-  if (e == cudaSuccess && rc == MFA_OK)  // dK, dV: k, v resident; q, dO streamed
-    e = launch_bwd_pass<true, kCausal, kBF16>(bp, k, v, q, dout, dk, dv, batch, heads, n,
-                                              layout, ctas, stream, &rc);
+  // A dK/dV step (two accumulators, two operand tiles) costs about kKvCost dQ steps.
+  // Many units per SM: one pass per launch, each over all SMs, units strided. Few (the last
+  // wave of a pass would leave >= 5% of the SMs idle): both passes in one launch on separate
+  // SMs, split to minimise the slower pass (equal units: ceil(units / CTAs) waves x cost;
+  // masked: units dealt out by length, about units / CTAs each).
+  constexpr double kKvCost = 1.05;
+  const double waves = static_cast<double>(units) / static_cast<double>(sms);
+  const bool together = sms >= 2 && std::ceil(waves) / waves > 1.05;
+  BwdParams pq = bp, pkv = bp;
+  pq.by_length = pkv.by_length = together && kCausal ? 1 : 0;
+  int64_t cq = sms, ckv = sms;  // CTAs per pass
+  if (together) {
+    double best = 1e300;
+    const double ideal = static_cast<double>(sms) / (1.0 + kKvCost);
+    for (int64_t c = 1; c < sms; ++c) {
+      const int64_t ck = sms - c;
+      const double tq = kCausal ? static_cast<double>(units) / c
+                                : static_cast<double>((units + c - 1) / c);
+      const double tk = kKvCost * (kCausal ? static_cast<double>(units) / ck
+                                           : static_cast<double>((units + ck - 1) / ck));
+      const double cost = tq > tk ? tq : tk;
+      const bool nearer = std::fabs(c - ideal) < std::fabs(cq - ideal);
+      if (cost < best * (1.0 - 1e-9) || (cost <= best * (1.0 + 1e-9) && nearer)) {
+        best = cost;
+        cq = c;
+      }
+    }
+    ckv = sms - cq;
+  }
+  if (cq > units) cq = units;
+  if (ckv > units) ckv = units;
+  // dQ: q, dO resident; k, v streamed. dK, dV: k, v resident; q, dO streamed.
+  rc = encode_bwd_pass<kBF16>(pq, q, dout, k, v, dq, nullptr, batch, heads, n, layout);
+  if (rc == MFA_OK)
+    rc = encode_bwd_pass<kBF16>(pkv, k, v, q, dout, dk, dv, batch, heads, n, layout);
+  constexpr int kThreads = BwdConfig<true, kCausal, kBF16>::kThreads;
+  constexpr int kSmem = bwd_smem_bytes<kCausal, kBF16>();
+  if (e == cudaSuccess && rc == MFA_OK) {
+    if (together) {
+      pq.cta0 = 0;
+      pq.ctas = static_cast<int>(cq);
+      pkv.cta0 = static_cast<int>(cq);
+      pkv.ctas = static_cast<int>(ckv);
+      mfa_bwd_kernel<kCausal, kBF16>
+          <<<static_cast<unsigned>(cq + ckv), kThreads, kSmem, stream>>>(pq, pkv);
+    } else {
+      pq.cta0 = pkv.cta0 = 0;
+      pq.ctas = static_cast<int>(cq);
+      pkv.ctas = static_cast<int>(ckv);
+      mfa_bwd_pass_kernel<false, kCausal, kBF16>
+          <<<static_cast<unsigned>(cq), kThreads, BwdConfig<false, kCausal, kBF16>::kSmemBytes,
+             stream>>>(pq);
+      e = cudaGetLastError();
+      if (e == cudaSuccess)
+        mfa_bwd_pass_kernel<true, kCausal, kBF16>
+            <<<static_cast<unsigned>(ckv), kThreads, BwdConfig<true, kCausal, kBF16>::kSmemBytes,
+               stream>>>(pkv);
+    }
+    e = cudaGetLastError();
+  }
   const cudaError_t ef = cudaFreeAsync(ws, stream);
   if (rc != MFA_OK) return rc;
   if (e == cudaSuccess) e = ef;
