@@ -361,8 +361,7 @@ __device__ __forceinline__ bool bwd_step(const BwdParams& p, uint8_t* smem, uint
   // [4i + e]: row g + 8 (e / 2), column 64 * half + 8i + 2q + e % 2 (tS, tDP already point at
   // this warp's column half)
   uint32_t sr[32], dp[32];
-  tmem_ld_16x256b_sync(tS, sr);
-  tmem_ld_16x256b_sync(tDP, dp);
+  tmem_ld2_16x256b_sync(tS, sr, tDP, dp);
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(bar(Cfg::kBarSSFree));
