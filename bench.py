@@ -50,7 +50,7 @@ PUBLISHED_TFLOPS = 4 * 8 * 8192 ** 2 * 64 / (PUBLISHED_TFLOPS * 1e-3) / 1e12
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 L2_FLUSH_MB = 256
 INPUT_BUFFERS = 4
-E2E_CHUNKS = 2  # measured best on this box: opposite-direction copies slow each other
+E2E_CHUNKS = 4  # pieces of decreasing size (forward_pinned): measured best
 
 WORKLOADS = {
     "b1h8n8192": dict(B=1, H=8, N=8192, dist="normal", qk_scale=1.0, scaling="weak"),

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <limits>
 #include <stdexcept>
+#include <string>
 #include <vector>
 
 #include "mfa_b200.h"
@@ -187,6 +188,102 @@ void flash_attn_forward_into(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
   launch_general(q, k, v, out, causal, Layout::kBHND);
 }
 
+// CUDA events of one pipelined call, destroyed on every exit path.
+struct EventSet {
+  std::vector<cudaEvent_t> ev;
+  explicit EventSet(size_t count) : ev(count, nullptr) {
+    for (auto& e : ev) {
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+        e = nullptr;
+        throw std::runtime_error("cudaEventCreateWithFlags failed");
+      }
+    }
+  }
+  ~EventSet() {
+    for (auto e : ev)
+      if (e) cudaEventDestroy(e);
+  }
+};
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// The host-buffer pipeline behind mini_flash_attention.forward_pinned in one call: q, k, v and
+// out are contiguous host tensors [rows, N, D] (pinned for overlap), `bounds` cuts the rows into
+// pieces. Piece i is copied in on one stream, computed on a second once it has arrived and
+// copied back on a third once it is computed, so the copies of neighbouring pieces overlap the
+// kernels. Returns when `out` holds the result. One plain cudaMemcpyAsync per tensor and piece.
+void flash_attn_forward_pinned(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                               torch::Tensor out, bool causal, std::vector<int64_t> bounds,
+                               int64_t device) {
+  for (const auto* x : {&q, &k, &v, &out}) {
+    TORCH_CHECK(!x->is_cuda(), "forward_pinned expects host tensors");
+    TORCH_CHECK(x->is_contiguous(), "host tensors must be contiguous");
+    TORCH_CHECK(x->dim() == 3, "host tensors must be [rows, N, D] views");
+    TORCH_CHECK(x->sizes() == q.sizes(), "k must have the same shape as q");
+    TORCH_CHECK(x->scalar_type() == q.scalar_type(), "k must have the same dtype as q");
+  }
+  TORCH_CHECK(q.scalar_type() == torch::kFloat16 || q.scalar_type() == torch::kBFloat16,
+              "q must be float16 or bfloat16");
+  const int64_t rows = q.size(0), n = q.size(1), d = q.size(2);
+  TORCH_CHECK(bounds.size() >= 2 && bounds.front() == 0 && bounds.back() == rows,
+              "bounds must run from 0 to the number of rows");
+  for (size_t i = 1; i < bounds.size(); ++i)
+    TORCH_CHECK(bounds[i] > bounds[i - 1], "bounds must increase");
+  if (rows == 0 || n == 0) return;
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  const auto opts = q.options().device(torch::kCUDA, static_cast<c10::DeviceIndex>(device));
+  auto dq = torch::empty({rows, n, d}, opts), dk = torch::empty({rows, n, d}, opts);
+  auto dv = torch::empty({rows, n, d}, opts), dout = torch::empty({rows, n, d}, opts);
+  const size_t pieces = bounds.size() - 1;
+  const cudaStream_t cur = at::cuda::getCurrentCUDAStream().stream();
+  const cudaStream_t s_in = at::cuda::getStreamFromPool().stream();
+  const cudaStream_t s_run = at::cuda::getStreamFromPool().stream();
+  const cudaStream_t s_out = at::cuda::getStreamFromPool().stream();
+  EventSet events(2 * pieces + 1);
+  // the device buffers come from the caching allocator on the current stream
+  check_cuda(cudaEventRecord(events.ev[2 * pieces], cur), "cudaEventRecord");
+  check_cuda(cudaStreamWaitEvent(s_in, events.ev[2 * pieces], 0), "cudaStreamWaitEvent");
+  const size_t row_bytes = static_cast<size_t>(n) * d * q.element_size();
+  const float scale = 1.0f / std::sqrt(static_cast<float>(d));
+  const int dtype = q.scalar_type() == torch::kBFloat16 ? MFA_DTYPE_BF16 : MFA_DTYPE_FP16;
+  auto at_row = [&](const torch::Tensor& x, int64_t r) {
+    return static_cast<char*>(x.data_ptr()) + static_cast<size_t>(r) * row_bytes;
+  };
+  int rc = MFA_OK;
+  for (size_t i = 0; i < pieces && rc == MFA_OK; ++i) {
+    const int64_t a = bounds[i], b = bounds[i + 1];
+    const size_t bytes = static_cast<size_t>(b - a) * row_bytes;
+    check_cuda(cudaMemcpyAsync(at_row(dq, a), at_row(q, a), bytes, cudaMemcpyHostToDevice, s_in),
+               "copy of q");
+    check_cuda(cudaMemcpyAsync(at_row(dk, a), at_row(k, a), bytes, cudaMemcpyHostToDevice, s_in),
+               "copy of k");
+    check_cuda(cudaMemcpyAsync(at_row(dv, a), at_row(v, a), bytes, cudaMemcpyHostToDevice, s_in),
+               "copy of v");
+    check_cuda(cudaEventRecord(events.ev[2 * i], s_in), "cudaEventRecord");
+    check_cuda(cudaStreamWaitEvent(s_run, events.ev[2 * i], 0), "cudaStreamWaitEvent");
+    rc = mfa_fwd(at_row(dq, a), at_row(dk, a), at_row(dv, a), at_row(dout, a), 1, b - a, n,
+                 static_cast<int32_t>(d), scale, causal ? 1 : 0, dtype, MFA_LAYOUT_BHND,
+                 static_cast<void*>(s_run));
+    if (rc != MFA_OK) break;
+    check_cuda(cudaEventRecord(events.ev[2 * i + 1], s_run), "cudaEventRecord");
+    check_cuda(cudaStreamWaitEvent(s_out, events.ev[2 * i + 1], 0), "cudaStreamWaitEvent");
+    check_cuda(cudaMemcpyAsync(at_row(out, a), at_row(dout, a), bytes, cudaMemcpyDeviceToHost,
+                               s_out),
+               "copy of the output");
+  }
+  // s_out waited for the last kernel, which waited for the last copies in: when it is done,
+  // every use of the device buffers is, and they may return to the allocator's current stream
+  const cudaError_t e_in = cudaStreamSynchronize(s_in);
+  const cudaError_t e_run = cudaStreamSynchronize(s_run);
+  const cudaError_t e_out = cudaStreamSynchronize(s_out);
+  if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
+  check_cuda(e_in, "copies in");
+  check_cuda(e_run, "forward");
+  check_cuda(e_out, "copies out");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -201,5 +298,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Mini Flash Attention forward, single-tile sm_100a kernel (replaces the WMMA path)");
   m.def("forward_into", &flash_attn_forward_into,
         "Mini Flash Attention forward into a preallocated output tensor");
+  m.def("forward_pinned", &flash_attn_forward_pinned,
+        "Pipelined forward on host tensors [rows, N, D] cut into pieces at `bounds`");
   m.def("version", []() { return std::string(mfa_version()); });
 }

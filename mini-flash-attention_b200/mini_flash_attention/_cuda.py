@@ -87,16 +87,37 @@ def forward_wmma(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool
     return _load_extension().forward_wmma(q, k, v, causal)
 
 
+def pinned_chunk_bounds(rows: int, chunks: int) -> list[int]:
+    """Row bounds of the pieces of ``forward_pinned``: ``chunks`` pieces of decreasing size
+    (weights 2^(c-2), ..., 2, 1, 1), every piece at least one row. The copy-in of all pieces
+    bounds the pipeline; small last pieces keep short the compute and copy-out that follow
+    it."""
+    chunks = max(1, min(chunks, rows))
+    weights = [2 ** (chunks - 2 - i) for i in range(chunks - 1)] + [1] if chunks > 1 else [1]
+    total = sum(weights)
+    bounds, acc = [0], 0
+    for i, w in enumerate(weights):
+        acc += w
+        b = rows * acc // total
+        b = max(b, bounds[-1] + 1)               # at least one row per piece
+        b = min(b, rows - (chunks - 1 - i))      # leave a row for every later piece
+        bounds.append(b)
+    bounds[-1] = rows
+    return bounds
+
+
 def forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                    out: torch.Tensor | None = None, chunks: int = 4,
                    device: torch.device | int | None = None) -> torch.Tensor:
-    """Attention forward on host tensors: fp16 q, k, v in (preferably pinned) CPU memory,
-    result written to a host tensor (``out`` or a new pinned one).
+    """Attention forward on host tensors: fp16 / bf16 q, k, v in (preferably pinned) CPU
+    memory, result written to a host tensor (``out`` or a new pinned one).
 
-    The batch*head rows are cut into ``chunks`` pieces that move through three CUDA streams:
-    piece i+1 is copied in while piece i is computed by ``forward`` and piece i-1 is copied
-    back, so the host<->device transfers overlap the kernels. Synchronous: returns when the
-    result is in ``out``. Same shape / dtype / error contract as ``forward``.
+    The batch*head rows are cut into ``chunks`` pieces of decreasing size
+    (``pinned_chunk_bounds``) that move through three CUDA streams: piece i+1 is copied in
+    while piece i is computed and piece i-1 is copied back, so the host<->device transfers
+    overlap the kernels. The pipeline runs in the C++ extension (one call, no per-piece Python
+    work). Synchronous: returns when the result is in ``out``. Same shape / dtype / error
+    contract as ``forward``.
     """
     if q.is_cuda or k.is_cuda or v.is_cuda:
         raise RuntimeError("forward_pinned expects host tensors; use forward for CUDA tensors")
@@ -112,6 +133,13 @@ def forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
         out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     if bh == 0 or n == 0:
         return out
+    if not out.is_contiguous():
+        raise RuntimeError("out must be contiguous")
+    q3, k3, v3 = (x.contiguous().reshape(bh, n, d) for x in (q, k, v))
+    o3 = out.reshape(bh, n, d)
+    _load_extension().forward_pinned(q3, k3, v3, o3, causal, pinned_chunk_bounds(bh, chunks),
+                                     dev.index)
+    return out
     q3, k3, v3, o3 = (x.reshape(bh, n, d) for x in (q, k, v, out))
     chunks = max(1, min(chunks, bh))
     bounds = [bh * i // chunks for i in range(chunks + 1)]
