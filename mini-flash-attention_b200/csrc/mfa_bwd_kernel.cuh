@@ -53,6 +53,7 @@ struct BwdParams {
   int cta0;
   int ctas;
   int by_length;  // causal only: deal units out by length (below), else strided
+  int reverse;    // CTA cta0 + c deals as CTA ctas - 1 - c (the second pass of a mixed launch)
 };
 
 template <bool kDKV_, bool kCausal_, bool kBF16_>
@@ -138,7 +139,8 @@ struct BwdCursor {
   // Unit of this CTA's k-th assignment, or -1 past the end.
   __device__ static int unit_at(const BwdParams& p, int k) {
     // units <= 2^31 - 2^16 (checked by the launcher), k * ctas <= units: 32-bit arithmetic
-    const int c = static_cast<int>(blockIdx.x) - p.cta0;
+    const int c0 = static_cast<int>(blockIdx.x) - p.cta0;
+    const int c = p.reverse ? p.ctas - 1 - c0 : c0;
     const int units = p.bh * p.blocks;
     if (!Cfg::kCausal || !p.by_length) {
       const int u = k * p.ctas + c;
@@ -333,6 +335,13 @@ __device__ __forceinline__ void bwd_mma_role(const BwdParams& p, uint8_t* smem, 
       ++gp;
       cp.step(p);
     }
+  }
+  // Every commit of this pass has arrived before the role returns (the barriers may be
+  // initialised again for a second pass).
+  if (issued_any) {
+    if (leader) mma_commit(bar(Cfg::kBarDrain));
+    __syncwarp();
+    wait_warp(bar(Cfg::kBarDrain), 0, wd, kSiteMmaDrain);  // on failure the CTA unwinds
   }
   return;
 
@@ -562,64 +571,114 @@ __device__ __forceinline__ void bwd_store_role(const BwdParams& p, uint8_t* smem
   tma_store_wait_read();
 }
 
-// One CTA of one pass.
+// The barriers of a CTA, initialised by one thread (the indices are those of both passes).
 template <class Cfg>
-__device__ __forceinline__ void bwd_cta(const BwdParams& p) {
+__device__ __forceinline__ void bwd_init_bars(uint32_t bars) {
+  for (int b = 0; b < 2; ++b) {
+    mbar_init(bars + 8 * (Cfg::kBarResFull + b), 1);
+    mbar_init(bars + 8 * (Cfg::kBarResEmpty + b), 1);
+  }
+  for (int s = 0; s < Cfg::STAGES; ++s) {
+    mbar_init(bars + 8 * (Cfg::kBarStrFull + s), 1);
+    mbar_init(bars + 8 * (Cfg::kBarStrEmpty + s), 1);
+  }
+  mbar_init(bars + 8 * Cfg::kBarSSFull, 1);
+  mbar_init(bars + 8 * Cfg::kBarSSFree, Cfg::kSoftmaxWarps);
+  mbar_init(bars + 8 * Cfg::kBarOpFull, Cfg::kSoftmaxWarps);
+  mbar_init(bars + 8 * Cfg::kBarAccDone, 1);
+  mbar_init(bars + 8 * Cfg::kBarStage, Cfg::kSoftmaxWarps);
+  mbar_init(bars + 8 * Cfg::kBarDrain, 1);
+  mbar_init_fence();
+}
+
+// One CTA: the units of pass CA (params pa), then, if kTwo, those of pass CB (params pb). Between
+// the passes every role has finished (the MMA warp drains its commits, the store thread waits
+// for its stores' shared-memory reads), the CTA meets on named barrier 2 and the barriers
+// start afresh; TMEM stays allocated. The barriers live past both passes' shared-memory
+// layouts. Each role's calls stay inside its setmaxnreg branch, which is what lets the
+// register allocator give the softmax-side warps their 104 registers.
+template <class CA, class CB, bool kTwo>
+__device__ __forceinline__ void bwd_cta(const BwdParams& pa, const BwdParams& pb) {
+  static_assert(CA::kNumBars == CB::kNumBars && CA::kThreads == CB::kThreads &&
+                    CA::kTmemCols == CB::kTmemCols,
+                "passes of one CTA share barriers, threads and TMEM");
+  constexpr int kBarOff = CA::kBarOff > CB::kBarOff ? CA::kBarOff : CB::kBarOff;
+  constexpr int kTmemSlotOff = kBarOff + CA::kNumBars * 8;
+  constexpr int kAbortOff = kTmemSlotOff + 4;
+  static_assert(kAbortOff + 4 + 1024 <= (CA::kSmemBytes > CB::kSmemBytes ? CA::kSmemBytes
+                                                                         : CB::kSmemBytes),
+                "barriers inside the launch's shared memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t bars = smem_addr(smem + Cfg::kBarOff);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kTmemSlotOff);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kAbortOff);
+  const uint32_t bars = smem_addr(smem + kBarOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTmemSlotOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
+  // Between the passes: true if the second pass runs (the same verdict in every thread:
+  // nothing writes the flag between the two barriers).
+  auto next_pass = [&]() -> bool {
+    __syncwarp();
+    tc_fence_before();
+    named_bar_sync(2, CA::kThreads);
+    tc_fence_after();
+    const bool go = *abort_flag == 0;
+    if (go && warp == CA::kLoadWarp && lane == 0) {
+      for (int i = 0; i < CA::kNumBars; ++i) mbar_inval(bars + 8 * i);
+      bwd_init_bars<CB>(bars);
+    }
+    named_bar_sync(2, CA::kThreads);
+    return go;
+  };
   // As in the forward kernel: the load thread initialises the barriers and goes straight on
   // to its first copies; the other warps wait on named barrier 1 for the barriers and warp
   // 0's TMEM allocation (the load warp only arrives there).
   uint32_t tmem = 0;
-  if (warp == Cfg::kLoadWarp) {
+  if (warp == CA::kLoadWarp) {
     if (lane == 0) {
       *abort_flag = 0;
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(bars + 8 * (Cfg::kBarResFull + b), 1);
-        mbar_init(bars + 8 * (Cfg::kBarResEmpty + b), 1);
-      }
-      for (int s = 0; s < Cfg::STAGES; ++s) {
-        mbar_init(bars + 8 * (Cfg::kBarStrFull + s), 1);
-        mbar_init(bars + 8 * (Cfg::kBarStrEmpty + s), 1);
-      }
-      mbar_init(bars + 8 * Cfg::kBarSSFull, 1);
-      mbar_init(bars + 8 * Cfg::kBarSSFree, Cfg::kSoftmaxWarps);
-      mbar_init(bars + 8 * Cfg::kBarOpFull, Cfg::kSoftmaxWarps);
-      mbar_init(bars + 8 * Cfg::kBarAccDone, 1);
-      mbar_init(bars + 8 * Cfg::kBarStage, Cfg::kSoftmaxWarps);
-      mbar_init(bars + 8 * Cfg::kBarDrain, 1);
-      mbar_init_fence();
+      bwd_init_bars<CA>(bars);
     }
     __syncwarp();
-    named_bar_arrive(1, Cfg::kThreads);
-    setmaxnreg_dec<Cfg::kControlRegs>();
-    const Watchdog wd{abort_flag, p.status, p.timeout_ns};
-    if (lane == 0) bwd_load_role<Cfg>(p, smem, bars, wd);
+    named_bar_arrive(1, CA::kThreads);
+    setmaxnreg_dec<CA::kControlRegs>();
+    const Watchdog wd{abort_flag, pa.status, pa.timeout_ns};
+    if (lane == 0) bwd_load_role<CA>(pa, smem, bars, wd);
+    if constexpr (kTwo) {
+      if (next_pass() && lane == 0) bwd_load_role<CB>(pb, smem, bars, wd);
+    }
   } else {
     if (warp == 0) {
-      tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
+      tmem_alloc(smem_addr(tmem_slot), CA::kTmemCols);
       tmem_relinquish();
     }
     tc_fence_before();
-    named_bar_sync(1, Cfg::kThreads);
+    named_bar_sync(1, CA::kThreads);
     tc_fence_after();
     tmem = *tmem_slot;
-    const Watchdog wd{abort_flag, p.status, p.timeout_ns};
-    if (warp < Cfg::kSoftmaxWarps) {
-      setmaxnreg_inc<Cfg::kSoftmaxRegs>();
-      bwd_softmax_role<Cfg>(p, smem, bars, tmem, wd);
+    const Watchdog wd{abort_flag, pa.status, pa.timeout_ns};
+    if (warp < CA::kSoftmaxWarps) {
+      setmaxnreg_inc<CA::kSoftmaxRegs>();
+      bwd_softmax_role<CA>(pa, smem, bars, tmem, wd);
+      if constexpr (kTwo) {
+        if (next_pass()) bwd_softmax_role<CB>(pb, smem, bars, tmem, wd);
+      }
     } else {
-      setmaxnreg_dec<Cfg::kControlRegs>();
-      if (warp == Cfg::kMmaWarp) {
-        bwd_mma_role<Cfg>(p, smem, bars, tmem, wd);
-      } else if (warp == Cfg::kStoreWarp) {
-        if (lane == 0) bwd_store_role<Cfg>(p, smem, bars, wd);
+      setmaxnreg_dec<CA::kControlRegs>();
+      if (warp == CA::kMmaWarp) {
+        bwd_mma_role<CA>(pa, smem, bars, tmem, wd);
+      } else if (warp == CA::kStoreWarp) {
+        if (lane == 0) bwd_store_role<CA>(pa, smem, bars, wd);
+      }
+      if constexpr (kTwo) {
+        if (next_pass()) {
+          if (warp == CB::kMmaWarp) {
+            bwd_mma_role<CB>(pb, smem, bars, tmem, wd);
+          } else if (warp == CB::kStoreWarp) {
+            if (lane == 0) bwd_store_role<CB>(pb, smem, bars, wd);
+          }
+        }
       }
     }
   }
@@ -627,22 +686,32 @@ __device__ __forceinline__ void bwd_cta(const BwdParams& p) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+  if (warp == 0) tmem_dealloc(tmem, CA::kTmemCols);
 }
 
 // Both passes in one launch, at the same time on separate SMs: CTAs [0, pkv.cta0) run the dQ
-// pass, the rest the dK/dV pass. Used when a pass has few units per SM (512 equal units of
-// one pass on 148 SMs ran 4 units on some SMs and 3 on others).
+// pass, the rest the dK/dV pass. Used when each pass has fewer units than about two per SM.
 template <bool kCausal, bool kBF16>
 __global__ void __launch_bounds__(BwdConfig<true, kCausal, kBF16>::kThreads, 1)
     mfa_bwd_kernel(const __grid_constant__ BwdParams pq, const __grid_constant__ BwdParams pkv) {
-  static_assert(BwdConfig<false, kCausal, kBF16>::kThreads ==
-                    BwdConfig<true, kCausal, kBF16>::kThreads,
-                "both passes run in one launch");
+  using CQ = BwdConfig<false, kCausal, kBF16>;
+  using CK = BwdConfig<true, kCausal, kBF16>;
   if (static_cast<int>(blockIdx.x) < pkv.cta0)
-    bwd_cta<BwdConfig<false, kCausal, kBF16>>(pq);
+    bwd_cta<CQ, CQ, false>(pq, pq);
   else
-    bwd_cta<BwdConfig<true, kCausal, kBF16>>(pkv);
+    bwd_cta<CK, CK, false>(pkv, pkv);
+}
+
+// Both passes in one launch, every CTA on both: its dK/dV units first, then its dQ units,
+// dealt from the other end of the grid (pq.reverse), so that the CTAs with one dK/dV unit
+// more than the others have none of the extra dQ units. Used when a pass has a few units
+// per SM: 512 units per pass on 148 SMs take 4 dK/dV + 3 dQ units on the slowest CTA, where
+// separate SMs per pass take 7 dK/dV units (a dK/dV step costs more than a dQ step).
+template <bool kCausal, bool kBF16>
+__global__ void __launch_bounds__(BwdConfig<true, kCausal, kBF16>::kThreads, 1)
+    mfa_bwd_mixed_kernel(const __grid_constant__ BwdParams pq,
+                         const __grid_constant__ BwdParams pkv) {
+  bwd_cta<BwdConfig<true, kCausal, kBF16>, BwdConfig<false, kCausal, kBF16>, true>(pkv, pq);
 }
 
 // One pass per launch (many units per SM), all CTAs on it; a kernel of its own, which measured
@@ -650,7 +719,8 @@ __global__ void __launch_bounds__(BwdConfig<true, kCausal, kBF16>::kThreads, 1)
 template <bool kDKV, bool kCausal, bool kBF16>
 __global__ void __launch_bounds__(BwdConfig<kDKV, kCausal, kBF16>::kThreads, 1)
     mfa_bwd_pass_kernel(const __grid_constant__ BwdParams p) {
-  bwd_cta<BwdConfig<kDKV, kCausal, kBF16>>(p);
+  using C = BwdConfig<kDKV, kCausal, kBF16>;
+  bwd_cta<C, C, false>(p, p);
 }
 
 // Dynamic shared memory of the two-pass launch.

@@ -52,6 +52,10 @@ cudaError_t set_bwd_attribute() {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        bwd_smem_bytes<kCausal, kBF16>());
   if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(mfa_bwd_mixed_kernel<kCausal, kBF16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             bwd_smem_bytes<kCausal, kBF16>());
+  if (e == cudaSuccess)
     e = cudaFuncSetAttribute(mfa_bwd_pass_kernel<false, kCausal, kBF16>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              BwdConfig<false, kCausal, kBF16>::kSmemBytes);
@@ -616,6 +620,57 @@ int encode_bwd_pass(BwdParams& bp, const void* x, const void* y, const void* s0,
   return MFA_OK;
 }
 
+// How the backward's two passes use the SMs (see launch_backward).
+struct BwdPlan {
+  enum Mode { kPasses, kSplit, kMixed } mode;
+  int64_t cq, ckv;  // CTAs of the dQ pass and the dK/dV pass (kMixed: the same CTAs)
+};
+
+BwdPlan plan_backward(int64_t units, int64_t sms, bool causal) {
+  constexpr double kKvCost = 1.05;    // a dK/dV step in dQ steps
+  constexpr double kRestart = 0.05;   // mixed: pipeline restart between passes, in units
+  const double waves = static_cast<double>(units) / static_cast<double>(sms);
+  if (sms < 2 || std::ceil(waves) / waves <= 1.05)
+    return {BwdPlan::kPasses, sms < units ? sms : units, sms < units ? sms : units};
+  double best = 1e300;
+  int64_t cq = sms;
+  const double ideal = static_cast<double>(sms) / (1.0 + kKvCost);
+  for (int64_t c = 1; c < sms; ++c) {
+    const int64_t ck = sms - c;
+    const double tq = causal ? static_cast<double>(units) / c
+                             : static_cast<double>((units + c - 1) / c);
+    const double tk = kKvCost * (causal ? static_cast<double>(units) / ck
+                                        : static_cast<double>((units + ck - 1) / ck));
+    const double cost = tq > tk ? tq : tk;
+    const bool nearer = std::fabs(c - ideal) < std::fabs(cq - ideal);
+    if (cost < best * (1.0 - 1e-9) || (cost <= best * (1.0 + 1e-9) && nearer)) {
+      best = cost;
+      cq = c;
+    }
+  }
+  const int64_t ckv = sms - cq;
+  // Mixed: CTA c takes units c, c + C, ... of the dK/dV pass and C - 1 - c, 2C - 1 - c, ...
+  // of the dQ pass, so the rem CTAs with an extra dK/dV unit get an extra dQ unit only when
+  // rem > C / 2. With at least one unit per SM it measured 2.6-4% faster than the split at
+  // every shape tried (256 and 512 units per pass, fp16, with and without the mask; the
+  // model's masked estimates of the two are within 0.1% of each other), so it is taken there
+  // outright; below that (each CTA then runs two units where a split CTA runs one) by the model.
+  const int64_t ctas = sms < units ? sms : units;
+  const int64_t base = units / ctas, rem = units % ctas;
+  double mixed;
+  if (causal)
+    mixed = static_cast<double>(units) * (1.0 + kKvCost) / static_cast<double>(ctas);
+  else if (rem == 0)
+    mixed = base * (1.0 + kKvCost);
+  else if (2 * rem <= ctas)
+    mixed = (base + 1) * kKvCost + base;
+  else
+    mixed = (base + 1) * (1.0 + kKvCost);
+  mixed += kRestart;
+  if (units >= sms || mixed < best) return {BwdPlan::kMixed, ctas, ctas};
+  return {BwdPlan::kSplit, cq < units ? cq : units, ckv < units ? ckv : units};
+}
+
 template <bool kCausal, bool kBF16>
 int launch_backward(const void* q, const void* k, const void* v, const void* out,
                     const void* dout, const float* lse, void* dq, void* dk, void* dv,
@@ -664,35 +719,17 @@ int launch_backward(const void* q, const void* k, const void* v, const void* out
   bp.status = g_devices[dev].status_ptr;
   // A dK/dV step (two accumulators, two operand tiles) costs about kKvCost dQ steps.
   // Many units per SM: one pass per launch, each over all SMs, units strided. Few (the last
-  // wave of a pass would leave >= 5% of the SMs idle): both passes in one launch on separate
-  // SMs, split to minimise the slower pass (equal units: ceil(units / CTAs) waves x cost;
-  // masked: units dealt out by length, about units / CTAs each).
-  constexpr double kKvCost = 1.05;
-  const double waves = static_cast<double>(units) / static_cast<double>(sms);
-  const bool together = sms >= 2 && std::ceil(waves) / waves > 1.05;
+  // wave of a pass would leave >= 5% of the SMs idle): both passes in one launch, either on
+  // separate SMs (split to minimise the slower pass: equal units take ceil(units / CTAs) x
+  // cost, masked ones dealt out by length about units / CTAs) or mixed, every CTA taking
+  // dK/dV units and then dQ units dealt from the other end of the grid, whichever the cost
+  // model finishes first (mixed pays a pipeline restart between its passes).
+  const BwdPlan plan = plan_backward(units, sms, kCausal);
   BwdParams pq = bp, pkv = bp;
-  pq.by_length = pkv.by_length = together && kCausal ? 1 : 0;
-  int64_t cq = sms, ckv = sms;  // CTAs per pass
-  if (together) {
-    double best = 1e300;
-    const double ideal = static_cast<double>(sms) / (1.0 + kKvCost);
-    for (int64_t c = 1; c < sms; ++c) {
-      const int64_t ck = sms - c;
-      const double tq = kCausal ? static_cast<double>(units) / c
-                                : static_cast<double>((units + c - 1) / c);
-      const double tk = kKvCost * (kCausal ? static_cast<double>(units) / ck
-                                           : static_cast<double>((units + ck - 1) / ck));
-      const double cost = tq > tk ? tq : tk;
-      const bool nearer = std::fabs(c - ideal) < std::fabs(cq - ideal);
-      if (cost < best * (1.0 - 1e-9) || (cost <= best * (1.0 + 1e-9) && nearer)) {
-        best = cost;
-        cq = c;
-      }
-    }
-    ckv = sms - cq;
-  }
-  if (cq > units) cq = units;
-  if (ckv > units) ckv = units;
+  pq.by_length = pkv.by_length = plan.mode != BwdPlan::kPasses && kCausal ? 1 : 0;
+  pq.reverse = plan.mode == BwdPlan::kMixed ? 1 : 0;
+  pkv.reverse = 0;
+  const int64_t cq = plan.cq, ckv = plan.ckv;
   // dQ: q, dO resident; k, v streamed. dK, dV: k, v resident; q, dO streamed.
   rc = encode_bwd_pass<kBF16>(pq, q, dout, k, v, dq, nullptr, batch, heads, n, layout);
   if (rc == MFA_OK)
@@ -700,13 +737,18 @@ int launch_backward(const void* q, const void* k, const void* v, const void* out
   constexpr int kThreads = BwdConfig<true, kCausal, kBF16>::kThreads;
   constexpr int kSmem = bwd_smem_bytes<kCausal, kBF16>();
   if (e == cudaSuccess && rc == MFA_OK) {
-    if (together) {
+    if (plan.mode == BwdPlan::kSplit) {
       pq.cta0 = 0;
       pq.ctas = static_cast<int>(cq);
       pkv.cta0 = static_cast<int>(cq);
       pkv.ctas = static_cast<int>(ckv);
       mfa_bwd_kernel<kCausal, kBF16>
           <<<static_cast<unsigned>(cq + ckv), kThreads, kSmem, stream>>>(pq, pkv);
+    } else if (plan.mode == BwdPlan::kMixed) {
+      pq.cta0 = pkv.cta0 = 0;
+      pq.ctas = pkv.ctas = static_cast<int>(cq);
+      mfa_bwd_mixed_kernel<kCausal, kBF16>
+          <<<static_cast<unsigned>(cq), kThreads, kSmem, stream>>>(pq, pkv);
     } else {
       pq.cta0 = pkv.cta0 = 0;
       pq.ctas = static_cast<int>(cq);

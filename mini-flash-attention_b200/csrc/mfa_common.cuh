@@ -53,6 +53,7 @@ enum WaitSite : int {
   kSiteLoadQEmpty = 13,
   kSiteSoftXch = 14,
   kSiteSoftStage = 15,
+  kSiteMmaDrain = 16,
 };
 
 // Head and batch index of a (batch * head) row.

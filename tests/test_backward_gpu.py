@@ -53,7 +53,7 @@ def check_grad(ours, ref, name):
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
 @pytest.mark.parametrize("B,H,N", [(1, 2, 128), (2, 1, 256), (1, 2, 2048), (2, 4, 1000),
-                                   (1, 8, 4096), (3, 3, 77)])
+                                   (1, 8, 4096), (3, 3, 77), (1, 3, 8000)])
 def test_backward_matches_autograd(B, H, N, dtype, causal):
     q, k, v, dout = (randn((B, H, N, 64), 300 + i, dtype) for i in range(4))
     out, lse = mfa.forward_lse(q, k, v, causal)
