@@ -251,34 +251,60 @@ void flash_attn_forward_pinned(torch::Tensor q, torch::Tensor k, torch::Tensor v
   auto at_row = [&](const torch::Tensor& x, int64_t r) {
     return static_cast<char*>(x.data_ptr()) + static_cast<size_t>(r) * row_bytes;
   };
+  // The first error stops further issue; the streams are drained before it is reported, so
+  // the device buffers never go back to the allocator while a copy or kernel still uses them.
   int rc = MFA_OK;
-  for (size_t i = 0; i < pieces && rc == MFA_OK; ++i) {
+  cudaError_t err = cudaSuccess;
+  const char* what = nullptr;
+  auto ok = [&](cudaError_t e, const char* w) {
+    if (err == cudaSuccess && e != cudaSuccess) {
+      err = e;
+      what = w;
+    }
+    return err == cudaSuccess;
+  };
+  // copies in (s_in) and forwards (s_run), piece by piece
+  size_t issued = 0;
+  for (size_t i = 0; i < pieces; ++i) {
     const int64_t a = bounds[i], b = bounds[i + 1];
     const size_t bytes = static_cast<size_t>(b - a) * row_bytes;
-    check_cuda(cudaMemcpyAsync(at_row(dq, a), at_row(q, a), bytes, cudaMemcpyHostToDevice, s_in),
-               "copy of q");
-    check_cuda(cudaMemcpyAsync(at_row(dk, a), at_row(k, a), bytes, cudaMemcpyHostToDevice, s_in),
-               "copy of k");
-    check_cuda(cudaMemcpyAsync(at_row(dv, a), at_row(v, a), bytes, cudaMemcpyHostToDevice, s_in),
-               "copy of v");
-    check_cuda(cudaEventRecord(events.ev[2 * i], s_in), "cudaEventRecord");
-    check_cuda(cudaStreamWaitEvent(s_run, events.ev[2 * i], 0), "cudaStreamWaitEvent");
+    if (!ok(cudaMemcpyAsync(at_row(dq, a), at_row(q, a), bytes, cudaMemcpyHostToDevice, s_in),
+            "copy of q") ||
+        !ok(cudaMemcpyAsync(at_row(dk, a), at_row(k, a), bytes, cudaMemcpyHostToDevice, s_in),
+            "copy of k") ||
+        !ok(cudaMemcpyAsync(at_row(dv, a), at_row(v, a), bytes, cudaMemcpyHostToDevice, s_in),
+            "copy of v") ||
+        !ok(cudaEventRecord(events.ev[2 * i], s_in), "cudaEventRecord") ||
+        !ok(cudaStreamWaitEvent(s_run, events.ev[2 * i], 0), "cudaStreamWaitEvent"))
+      break;
     rc = mfa_fwd(at_row(dq, a), at_row(dk, a), at_row(dv, a), at_row(dout, a), 1, b - a, n,
                  static_cast<int32_t>(d), scale, causal ? 1 : 0, dtype, MFA_LAYOUT_BHND,
                  static_cast<void*>(s_run));
-    if (rc != MFA_OK) break;
-    check_cuda(cudaEventRecord(events.ev[2 * i + 1], s_run), "cudaEventRecord");
-    check_cuda(cudaStreamWaitEvent(s_out, events.ev[2 * i + 1], 0), "cudaStreamWaitEvent");
-    check_cuda(cudaMemcpyAsync(at_row(out, a), at_row(dout, a), bytes, cudaMemcpyDeviceToHost,
-                               s_out),
-               "copy of the output");
+    if (rc != MFA_OK || !ok(cudaEventRecord(events.ev[2 * i + 1], s_run), "cudaEventRecord"))
+      break;
+    issued = i + 1;
   }
-  // s_out waited for the last kernel, which waited for the last copies in: when it is done,
-  // every use of the device buffers is, and they may return to the allocator's current stream
+  // copies out (s_out), each after its piece's forward. When a copy out overlaps copies in,
+  // the copy out takes the larger share of PCIe (measured: ~40 of ~60 GB/s), so the
+  // second-to-last piece's copy waits until the last piece is in: it then runs while the last
+  // forward does, and the last piece reaches the GPU sooner.
+  for (size_t i = 0; i < issued; ++i) {
+    const int64_t a = bounds[i], b = bounds[i + 1];
+    const size_t bytes = static_cast<size_t>(b - a) * row_bytes;
+    if (!ok(cudaStreamWaitEvent(s_out, events.ev[2 * i + 1], 0), "cudaStreamWaitEvent") ||
+        (i + 2 == pieces && issued == pieces &&
+         !ok(cudaStreamWaitEvent(s_out, events.ev[2 * (pieces - 1)], 0), "cudaStreamWaitEvent")) ||
+        !ok(cudaMemcpyAsync(at_row(out, a), at_row(dout, a), bytes, cudaMemcpyDeviceToHost, s_out),
+            "copy of the output"))
+      break;
+  }
+  // Every use of the device buffers is on these three streams: once they are drained the
+  // buffers may return to the allocator's current stream.
   const cudaError_t e_in = cudaStreamSynchronize(s_in);
   const cudaError_t e_run = cudaStreamSynchronize(s_run);
   const cudaError_t e_out = cudaStreamSynchronize(s_out);
   if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
+  check_cuda(err, what ? what : "");
   check_cuda(e_in, "copies in");
   check_cuda(e_run, "forward");
   check_cuda(e_out, "copies out");
