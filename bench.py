@@ -368,7 +368,8 @@ def run_ours(args, wl) -> dict | None:
     bytes_in = 3 * global_bh * n * d * 2
     bytes_out = global_bh * n * d * 2
     line = {
-        "metric": METRIC,
+        "metric": METRIC if not train else
+        "training-step TFLOPS/GPU (3.5·4·BH·N²·D/t: forward with log-sum-exp + backward)",
         "value": round(value, 3),
         "unit": UNIT,
         "n_gpus": world,
