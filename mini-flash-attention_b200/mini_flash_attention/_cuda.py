@@ -140,27 +140,3 @@ def forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     _load_extension().forward_pinned(q3, k3, v3, o3, causal, pinned_chunk_bounds(bh, chunks),
                                      dev.index)
     return out
-    q3, k3, v3, o3 = (x.reshape(bh, n, d) for x in (q, k, v, out))
-    chunks = max(1, min(chunks, bh))
-    bounds = [bh * i // chunks for i in range(chunks + 1)]
-    with torch.cuda.device(dev):
-        s_in, s_run, s_out = (torch.cuda.Stream(dev) for _ in range(3))
-        dq, dk, dv, do = (torch.empty((bh, n, d), dtype=q.dtype, device=dev) for _ in range(4))
-        ev_in = [torch.cuda.Event() for _ in range(chunks)]
-        ev_run = [torch.cuda.Event() for _ in range(chunks)]
-        ext = _load_extension()
-        for i in range(chunks):
-            a, b = bounds[i], bounds[i + 1]
-            with torch.cuda.stream(s_in):
-                for src, dst in ((q3, dq), (k3, dk), (v3, dv)):
-                    dst[a:b].copy_(src[a:b], non_blocking=True)
-                ev_in[i].record(s_in)
-            with torch.cuda.stream(s_run):
-                s_run.wait_event(ev_in[i])
-                ext.forward_into(dq[a:b], dk[a:b], dv[a:b], do[a:b], causal)
-                ev_run[i].record(s_run)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_run[i])
-                o3[a:b].copy_(do[a:b], non_blocking=True)
-        s_out.synchronize()  # every stream's work on the device buffers is done here
-    return out
