@@ -57,6 +57,9 @@ WORKLOADS = {
     "b16h16n4096": dict(B=16, H=16, N=4096, dist="normal", qk_scale=1.0, scaling="strong"),
     "b1h32n32768": dict(B=1, H=32, N=32768, dist="normal", qk_scale=3.0, scaling="strong"),
     "b128h16n512": dict(B=128, H=16, N=512, dist="uniform", qk_scale=1.0, scaling="strong"),
+    # not a reference configuration: one head, so that 2 or more GPUs split its query rows
+    # (sharding.q_shard, forward_rows) with the whole k and v on every GPU
+    "b1h1n65536": dict(B=1, H=1, N=65536, dist="normal", qk_scale=1.0, scaling="strong"),
 }
 D = 64
 
@@ -191,14 +194,29 @@ def make_inputs(wl: dict, bh: int, seed: int, device, d: int = D, dtype=torch.fl
 
 
 # ---------------------------------------------------------------- CPU baseline
+CPU_SAMPLE_ROWS = 4096  # query rows of one head timed on the host when N is long
+
+
+def cpu_sample(wl: dict, causal: bool = False):
+    """(q, k, v, flops, text): one head of the workload for the host-core timing; for N above
+    16384 without the mask only its first CPU_SAMPLE_ROWS query rows (against all N keys), so
+    that the fp32 score matrix stays within a few GB."""
+    q, k, v = make_inputs(wl, 1, 0, "cpu")
+    n = wl["N"]
+    if causal or n <= 16384:
+        return q, k, v, attention_flops(1, n, causal=causal), f"[1,{n},64]"
+    rows = CPU_SAMPLE_ROWS
+    return (q[:, :rows].contiguous(), k, v, 4.0 * rows * n * D,
+            f"query rows 0-{rows - 1} of [1,{n},64] against all {n} keys")
+
+
 def cpu_baseline(wl: dict, budget_s: float = 10.0, causal: bool = False) -> dict:
     """The reference's naive torch attention on the host cores, one head of the workload."""
     from oracle.torch_naive import torch_naive_attention
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    q, k, v = make_inputs(wl, 1, 0, "cpu")
-    flops = attention_flops(1, wl["N"], causal=causal)
+    q, k, v, flops, what = cpu_sample(wl, causal)
     times = []
     t_end = time.perf_counter() + budget_s
     while True:
@@ -210,7 +228,7 @@ def cpu_baseline(wl: dict, budget_s: float = 10.0, causal: bool = False) -> dict
     t = statistics.median(times)
     return {"value": flops / t / 1e12, "unit": UNIT, "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"1 of {wl['B'] * wl['H']} heads ([1,{wl['N']},64]), naive fp32 torch "
+            "sample": f"1 of {wl['B'] * wl['H']} heads ({what}), naive fp32 torch "
                       f"attention (benchs/benchmark_forward.py:98-115), median of {len(times)} "
                       f"runs in {sum(times):.1f} s"}
 
@@ -267,21 +285,26 @@ def max_over_ranks(x: float, world: int) -> float:
 
 def run_ours(args, wl) -> dict | None:
     import mini_flash_attention as mfa
-    from mini_flash_attention.sharding import bh_shard
+    from mini_flash_attention.sharding import bh_shard, q_shard, shard_mode
 
     rank, world, local = init_dist()
     dev = torch.device("cuda", local)
-    if wl["scaling"] == "weak":
-        global_bh = wl["B"] * wl["H"] * world
-        shard = bh_shard(global_bh, rank, world)
-    else:
-        global_bh = wl["B"] * wl["H"]
-        shard = bh_shard(global_bh, rank, world)
-    bh = shard.rows
+    global_bh = wl["B"] * wl["H"] * (world if wl["scaling"] == "weak" else 1)
     n = wl["N"]
     d = args.head_dim
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
     train = args.mode == "fwd_bwd"
+    q_range = None
+    if shard_mode(global_bh, world) == "rows":
+        bh = bh_shard(global_bh, rank, world).rows
+    else:
+        # fewer batch*head rows than GPUs: every rank holds the whole q, k, v and computes a
+        # range of query rows of every head
+        if train or args.causal:
+            raise SystemExit("query-row sharding (B*H < GPUs) is forward-only and non-causal")
+        bh = global_bh
+        qs = q_shard(n, rank, world)
+        q_range = (qs.begin, qs.end)
     inputs = [make_inputs(wl, bh, rank * INPUT_BUFFERS + i, dev, d, dtype, with_grad=train)
               for i in range(INPUT_BUFFERS)]
     flush = torch.empty(L2_FLUSH_MB * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
@@ -292,9 +315,14 @@ def run_ours(args, wl) -> dict | None:
         def fwd(q, k, v, do):
             out, lse = mfa.forward_lse(q, k, v, causal=causal)
             return mfa.backward(q, k, v, out, lse, do, causal=causal)
-    else:
+    elif q_range is None:
         def fwd(q, k, v):
             return mfa.forward(q, k, v, causal=causal)
+    else:
+        rows_out = torch.empty_like(inputs[0][0])
+
+        def fwd(q, k, v):
+            return mfa.forward_rows(q, k, v, q_range[0], q_range[1], out=rows_out)
 
     stream = torch.cuda.current_stream(dev)
 
@@ -330,7 +358,7 @@ def run_ours(args, wl) -> dict | None:
         # through the public host-buffer API (copies of batch*head slices overlap kernels)
         e2e_steps = max(args.steps, 3)
         e2e_ms = None
-        if not train:
+        if not train and q_range is None:
             host_in = [x.cpu().pin_memory() for x in inputs[0]]
             host_out = torch.empty(inputs[0][0].shape, dtype=dtype).pin_memory()
             chunks = min(bh, E2E_CHUNKS)
@@ -357,6 +385,8 @@ def run_ours(args, wl) -> dict | None:
     # a training step counts the forward (2 products) and the backward (5 products)
     flop_mult = 3.5 if train else 1.0
     flops_rank_step = flop_mult * attention_flops(bh, n, d, causal=causal)
+    if q_range is not None:  # this rank's query rows attend to all n keys
+        flops_rank_step *= (q_range[1] - q_range[0]) / n
     job_flops_step = flop_mult * attention_flops(global_bh, n, d, causal=causal)
     value = job_flops_step * args.steps / (total_ms / 1e3) / 1e12
     kernel_ms = total_ms / args.steps
@@ -386,7 +416,10 @@ def run_ours(args, wl) -> dict | None:
             "workload": args.workload,
             "B": wl["B"] * (world if wl["scaling"] == "weak" else 1), "H": wl["H"], "N": n,
             "D": d, "bh_per_gpu": bh, "causal": causal, "mode": args.mode,
-            "parallelism": f"batch*head sharded over {world} GPU(s), no collective",
+            "parallelism": (f"batch*head sharded over {world} GPU(s), no collective"
+                            if q_range is None else
+                            f"query rows of every head sharded over {world} GPU(s) (whole k, v "
+                            "on each), no collective"),
             "l2": f"{L2_FLUSH_MB} MB write before every step, outside the timed interval",
             "input_buffers": INPUT_BUFFERS,
             "timing": "CUDA events around each forward() call on its stream, max over ranks",
@@ -412,7 +445,9 @@ def run_ours(args, wl) -> dict | None:
             "path": "mini_flash_attention.forward_pinned: pinned host q,k,v -> H2D / forward / "
                     "D2H of batch*head slices pipelined on 3 streams -> pinned host out",
             "timing": "host wall clock around the synchronous calls, max over ranks",
-        } if e2e_value is not None else {"value": None, "reason": "no host-buffer training API"}),
+        } if e2e_value is not None else {"value": None, "reason": (
+            "no host-buffer training API" if train else
+            "forward_pinned has no query-row range")}),
         "gpu_launches": None if per_call is None else per_call * args.steps,
         "gpu_kernels": kernel_names,
         "clocks": clocks,
@@ -433,7 +468,7 @@ def run_reference(args, wl) -> dict | None:
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    q, k, v = make_inputs(wl, 1, 0, "cpu")
+    q, k, v, flops, what = cpu_sample(wl)
     for _ in range(args.warmup):
         torch_naive_attention(q, k, v)
     times = []
@@ -442,8 +477,8 @@ def run_reference(args, wl) -> dict | None:
         torch_naive_attention(q, k, v)
         times.append(time.perf_counter() - t0)
     total = sum(times)
-    value = attention_flops(1, wl["N"]) * args.steps / total / 1e12
-    sample = (f"1 of {wl['B'] * wl['H']} heads ([1,{wl['N']},64]) per step, naive fp32 torch "
+    value = flops * args.steps / total / 1e12
+    sample = (f"1 of {wl['B'] * wl['H']} heads ({what}) per step, naive fp32 torch "
               f"attention (benchs/benchmark_forward.py:98-115) on {threads} host threads")
     return {
         "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": 0,

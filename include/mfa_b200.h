@@ -84,6 +84,19 @@ MFA_API int mfa_fwd(const void* q, const void* k, const void* v, void* out, int6
                     int32_t dtype, int32_t layout, void* stream);
 
 /*
+ * mfa_fwd restricted to the query rows [q_begin, q_end) of every head: q, k, v and out are the
+ * whole tensors (as for mfa_fwd), every query row in the range attends to all N keys, and only
+ * those rows of out are written. For multi-GPU sharding when B*H is smaller than the number of
+ * GPUs: each GPU holds the whole k and v and takes a range of query rows. Non-causal only
+ * (causal != 0 with a range other than [0, N): MFA_ERR_INVALID_ARGUMENT); 0 <= q_begin <=
+ * q_end <= N. No counterpart in the reference, which has no multi-GPU mode.
+ */
+MFA_API int mfa_fwd_rows(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                         int64_t heads, int64_t n, int64_t q_begin, int64_t q_end, int32_t d,
+                         float scale, int32_t causal, int32_t dtype, int32_t layout,
+                         void* stream);
+
+/*
  * mfa_fwd that also writes the row log-sum-exp of the scaled scores,
  * lse[bh * N + row] = ln(sum over keys of exp(scale * q.k)), fp32 [B*H, N] whatever the
  * layout: the state the backward pass needs. No counterpart in the reference (no backward).

@@ -188,6 +188,26 @@ void flash_attn_forward_into(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
   launch_general(q, k, v, out, causal, Layout::kBHND);
 }
 
+// Query rows [q_begin, q_end) of every head of out ([B, H, N, D] or [B*H, N, D], the shape of
+// q), each against all N keys; the other rows of out are left as they are. Non-causal.
+void flash_attn_forward_rows(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
+                             int64_t q_begin, int64_t q_end) {
+  check_forward_inputs(q, k, v, true, Layout::kBHND);
+  TORCH_CHECK(out.is_cuda() && out.device() == q.device(), "out must be on q's device");
+  TORCH_CHECK(out.scalar_type() == q.scalar_type(), "out must have q's dtype");
+  TORCH_CHECK(out.is_contiguous(), "out must be contiguous");
+  TORCH_CHECK(out.sizes() == q.sizes(), "out must have the same shape as q");
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  const Extents e = extents_of(q, Layout::kBHND);
+  const float scale = 1.0f / std::sqrt(static_cast<float>(e.d));
+  const int dtype = q.scalar_type() == torch::kBFloat16 ? MFA_DTYPE_BF16 : MFA_DTYPE_FP16;
+  const int rc = mfa_fwd_rows(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), e.batch,
+                              e.heads, e.n, q_begin, q_end, static_cast<int32_t>(e.d), scale, 0,
+                              dtype, MFA_LAYOUT_BHND,
+                              static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
+  if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
+}
+
 // CUDA events of one pipelined call, destroyed on every exit path.
 struct EventSet {
   std::vector<cudaEvent_t> ev;
@@ -324,6 +344,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Mini Flash Attention forward, single-tile sm_100a kernel (replaces the WMMA path)");
   m.def("forward_into", &flash_attn_forward_into,
         "Mini Flash Attention forward into a preallocated output tensor");
+  m.def("forward_rows", &flash_attn_forward_rows,
+        "Forward of the query rows [q_begin, q_end) of every head into out (non-causal)");
   m.def("forward_pinned", &flash_attn_forward_pinned,
         "Pipelined forward on host tensors [rows, N, D] cut into pieces at `bounds`");
   m.def("version", []() { return std::string(mfa_version()); });

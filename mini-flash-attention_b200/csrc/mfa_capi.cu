@@ -192,13 +192,15 @@ Strides layout_strides(int layout, int64_t heads, int64_t n, int64_t d) {
 // 4-D TMA view {D, N, H, B} of one tensor, box {min(D, 64), 128, 1, 1}: 128-byte swizzle for
 // 64-column boxes, 64-byte swizzle for D = 32. The N extent keeps tiles inside their head:
 // rows past N read as zero and are not stored.
+// `rows` (default n) rows per head starting at `base`; the strides are those of an N = n tensor.
 int encode_tensor(CUtensorMap* map, const void* base, int64_t batch, int64_t heads, int64_t n,
-                  int64_t d, int layout, bool bf16) {
+                  int64_t d, int layout, bool bf16, int64_t rows = -1) {
   std::string why;
   auto encode = tensor_map_encoder(&why);
   if (!encode) return fail(MFA_ERR_CUDA, why);
   const Strides st = layout_strides(layout, heads, n, d);
-  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(n),
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(d),
+                              static_cast<cuuint64_t>(rows < 0 ? n : rows),
                               static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
   const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st.n) * 2,
                                  static_cast<cuuint64_t>(st.h) * 2,
@@ -249,15 +251,16 @@ struct Plan {
   size_t workspace_bytes = 0;  // split mode: partial-result slots
 };
 
+// nq query rows and n keys per head (nq == n but for a row range).
 template <class Cfg>
-int plan_forward(int64_t bh, int64_t n, int64_t sms, Plan& pl) {
-  const int64_t q_blocks = (n + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
+int plan_forward(int64_t bh, int64_t nq, int64_t n, int64_t sms, Plan& pl) {
+  const int64_t q_blocks = (nq + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
   const int64_t nkb = (n + Cfg::kKeys - 1) / Cfg::kKeys;
   const int64_t units = q_blocks * bh;
   if (static_cast<double>(units) * static_cast<double>(nkb) > static_cast<double>(int64_t(1) << 40) ||
       units > 0x7fffffffLL)
     return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  pl.sc = make_schedule(bh, n, Cfg::kRowsPerUnit, Cfg::kKeys, Cfg::kCausal);
+  pl.sc = make_schedule(bh, nq, n, Cfg::kRowsPerUnit, Cfg::kKeys, Cfg::kCausal);
   const int64_t total = pl.sc.total();
   pl.ctas = units < sms ? units : sms;
   pl.split = 0;
@@ -281,24 +284,31 @@ int plan_forward(int64_t bh, int64_t n, int64_t sms, Plan& pl) {
 
 // Queues the forward kernel (and the merge kernel in split mode) of plan `pl` on `stream`;
 // `workspace` holds pl.workspace_bytes.
+// Query rows [q_begin, q_end) of every head (all of them by default) against all n keys.
 template <class Cfg>
 cudaError_t launch_planned(const void* q, const void* k, const void* v, void* out, int64_t batch,
                            int64_t heads, int64_t n, int layout, float scale, const Plan& pl,
                            float* workspace, int* status_ptr, cudaStream_t stream, int* rc,
-                           float* lse = nullptr) {
+                           float* lse = nullptr, int64_t q_begin = 0, int64_t q_end = -1) {
   FwdParams p;
   *rc = MFA_OK;
   const bool bf16 = Cfg::kBF16;
   const int64_t d = Cfg::kHeadDim;
-  if ((*rc = encode_tensor(&p.tm_q, q, batch, heads, n, d, layout, bf16)) != MFA_OK)
+  const int64_t nq = (q_end < 0 ? n : q_end) - q_begin;
+  const Strides st = layout_strides(layout, heads, n, d);
+  const size_t row_off = static_cast<size_t>(q_begin) * static_cast<size_t>(st.n) * 2;  // bytes
+  const void* q_rows = static_cast<const char*>(q) + row_off;
+  void* out_rows = static_cast<char*>(out) + row_off;
+  if ((*rc = encode_tensor(&p.tm_q, q_rows, batch, heads, n, d, layout, bf16, nq)) != MFA_OK)
     return cudaSuccess;
   if ((*rc = encode_tensor(&p.tm_k, k, batch, heads, n, d, layout, bf16)) != MFA_OK)
     return cudaSuccess;
   if ((*rc = encode_tensor(&p.tm_v, v, batch, heads, n, d, layout, bf16)) != MFA_OK)
     return cudaSuccess;
-  if ((*rc = encode_tensor(&p.tm_o, out, batch, heads, n, d, layout, bf16)) != MFA_OK)
+  if ((*rc = encode_tensor(&p.tm_o, out_rows, batch, heads, n, d, layout, bf16, nq)) != MFA_OK)
     return cudaSuccess;
   p.n = static_cast<int>(n);
+  p.nq = static_cast<int>(nq);
   p.heads = static_cast<int>(heads);
   p.sc = pl.sc;
   p.split = pl.split;
@@ -311,12 +321,12 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
       <<<static_cast<unsigned>(pl.ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && pl.split) {
-    const Strides st = layout_strides(layout, heads, n, d);
     MergeParams mp;
-    mp.out = out;
+    mp.out = out_rows;
     mp.lse = lse;
     mp.workspace = workspace;
     mp.n = p.n;
+    mp.nq = p.nq;
     mp.heads = p.heads;
     mp.stride_b = st.b;
     mp.stride_h = st.h;
@@ -333,9 +343,10 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
 template <class Cfg>
 int launch_forward(const void* q, const void* k, const void* v, void* out, int64_t batch,
                    int64_t heads, int64_t n, int layout, float scale, cudaStream_t stream,
-                   float* lse = nullptr) {
+                   float* lse = nullptr, int64_t q_begin = 0, int64_t q_end = -1) {
   const int64_t bh = batch * heads;
-  if (bh == 0 || n == 0) return MFA_OK;
+  if (q_end < 0) q_end = n;
+  if (bh == 0 || n == 0 || q_end == q_begin) return MFA_OK;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
@@ -343,7 +354,8 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
   if (rc != MFA_OK) return rc;
   if ((rc = check_device_pointers(q, k, v, out, dev)) != MFA_OK) return rc;
   Plan pl;
-  if ((rc = plan_forward<Cfg>(bh, n, g_devices[dev].num_sms, pl)) != MFA_OK) return rc;
+  if ((rc = plan_forward<Cfg>(bh, q_end - q_begin, n, g_devices[dev].num_sms, pl)) != MFA_OK)
+    return rc;
   float* workspace = nullptr;
   if (pl.split) {
     e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&workspace), pl.workspace_bytes,
@@ -351,7 +363,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
     if (e != cudaSuccess) return fail_cuda(e, "cudaMallocFromPoolAsync (split workspace)");
   }
   e = launch_planned<Cfg>(q, k, v, out, batch, heads, n, layout, scale, pl, workspace,
-                          g_devices[dev].status_ptr, stream, &rc, lse);
+                          g_devices[dev].status_ptr, stream, &rc, lse, q_begin, q_end);
   if (pl.split) {
     const cudaError_t ef = cudaFreeAsync(workspace, stream);
     if (e == cudaSuccess) e = ef;
@@ -465,7 +477,7 @@ int launch_forward_noalloc(const void* q, const void* k, const void* v, void* ou
   if ((rc = check_device_pointers(q, k, v, out, dev)) != MFA_OK) return rc;
   const NoAllocState& st = g_noalloc[dev];
   Plan pl;
-  if ((rc = plan_forward<Cfg>(bh, n, st.num_sms, pl)) != MFA_OK) return rc;
+  if ((rc = plan_forward<Cfg>(bh, n, n, st.num_sms, pl)) != MFA_OK) return rc;
   // Every slot the merge kernel reads is written by the forward kernel of the same call, so
   // nothing in the scratch has to start at zero.
   if (pl.workspace_bytes > MFA_NOALLOC_SCRATCH_BYTES)
@@ -552,32 +564,35 @@ namespace {
 template <int D, bool kLSE>
 int launch_general_l(const void* q, const void* k, const void* v, void* out, int64_t batch,
                      int64_t heads, int64_t n, float scale, int32_t causal, int32_t dtype,
-                     int32_t layout, cudaStream_t s, float* lse) {
+                     int32_t layout, cudaStream_t s, float* lse, int64_t q_begin,
+                     int64_t q_end) {
   if (dtype == MFA_DTYPE_BF16)
     return causal ? launch_forward<Full<true, true, D, kLSE>>(q, k, v, out, batch, heads, n,
-                                                              layout, scale, s, lse)
+                                                              layout, scale, s, lse, q_begin, q_end)
                   : launch_forward<Full<false, true, D, kLSE>>(q, k, v, out, batch, heads, n,
-                                                               layout, scale, s, lse);
+                                                               layout, scale, s, lse, q_begin, q_end);
   return causal ? launch_forward<Full<true, false, D, kLSE>>(q, k, v, out, batch, heads, n,
-                                                             layout, scale, s, lse)
+                                                             layout, scale, s, lse, q_begin, q_end)
                 : launch_forward<Full<false, false, D, kLSE>>(q, k, v, out, batch, heads, n,
-                                                              layout, scale, s, lse);
+                                                              layout, scale, s, lse, q_begin, q_end);
 }
 
 // The row log-sum-exp is a compile-time option: the plain forward kernels carry none of it.
 template <int D>
 int launch_general(const void* q, const void* k, const void* v, void* out, int64_t batch,
                    int64_t heads, int64_t n, float scale, int32_t causal, int32_t dtype,
-                   int32_t layout, cudaStream_t s, float* lse) {
+                   int32_t layout, cudaStream_t s, float* lse, int64_t q_begin = 0,
+                   int64_t q_end = -1) {
   return lse ? launch_general_l<D, true>(q, k, v, out, batch, heads, n, scale, causal, dtype,
-                                         layout, s, lse)
+                                         layout, s, lse, q_begin, q_end)
              : launch_general_l<D, false>(q, k, v, out, batch, heads, n, scale, causal, dtype,
-                                          layout, s, nullptr);
+                                          layout, s, nullptr, q_begin, q_end);
 }
 
 int fwd_general(const void* q, const void* k, const void* v, void* out, float* lse,
                 int64_t batch, int64_t heads, int64_t n, int32_t d, float scale, int32_t causal,
-                int32_t dtype, int32_t layout, void* stream) {
+                int32_t dtype, int32_t layout, void* stream, int64_t q_begin = 0,
+                int64_t q_end = -1) {
   if (batch < 0 || heads < 0) return fail(MFA_ERR_INVALID_ARGUMENT, "negative extent");
   if (heads > 0 && batch > 0x7fffffffLL / heads)
     return fail(MFA_ERR_INVALID_ARGUMENT, "B * H is too large");
@@ -595,13 +610,22 @@ int fwd_general(const void* q, const void* k, const void* v, void* out, float* l
     if (reinterpret_cast<uintptr_t>(lse) & 3u)
       return fail(MFA_ERR_INVALID_ARGUMENT, "lse must be 4-byte aligned");
   }
+  if (q_end < 0) q_end = n;
+  if (q_begin < 0 || q_begin > q_end || q_end > n)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "query rows must satisfy 0 <= q_begin <= q_end <= N");
+  if (causal && (q_begin != 0 || q_end != n))
+    return fail(MFA_ERR_INVALID_ARGUMENT, "a query row range needs causal = 0");
+  if (lse != nullptr && (q_begin != 0 || q_end != n))
+    return fail(MFA_ERR_INVALID_ARGUMENT, "a query row range writes no log-sum-exp");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (d == 32)
-    return launch_general<32>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s, lse);
+    return launch_general<32>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s, lse,
+                              q_begin, q_end);
   if (d == 128)
     return launch_general<128>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s,
-                               lse);
-  return launch_general<64>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s, lse);
+                               lse, q_begin, q_end);
+  return launch_general<64>(q, k, v, out, batch, heads, n, scale, causal, dtype, layout, s, lse,
+                            q_begin, q_end);
 }
 
 // ---------------------------------------------------------------- backward
@@ -779,6 +803,14 @@ extern "C" int mfa_fwd(const void* q, const void* k, const void* v, void* out, i
                        int32_t dtype, int32_t layout, void* stream) {
   return fwd_general(q, k, v, out, nullptr, batch, heads, n, d, scale, causal, dtype, layout,
                      stream);
+}
+
+extern "C" int mfa_fwd_rows(const void* q, const void* k, const void* v, void* out,
+                            int64_t batch, int64_t heads, int64_t n, int64_t q_begin,
+                            int64_t q_end, int32_t d, float scale, int32_t causal, int32_t dtype,
+                            int32_t layout, void* stream) {
+  return fwd_general(q, k, v, out, nullptr, batch, heads, n, d, scale, causal, dtype, layout,
+                     stream, q_begin, q_end);
 }
 
 extern "C" int mfa_fwd_lse(const void* q, const void* k, const void* v, void* out, float* lse,

@@ -611,7 +611,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
         for (int r = 0; r < 2; ++r) {
           const int qrow = p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows +
                            slice + gq + 8 * r;
-          if (qrow < p.n)
+          if (qrow < p.nq)
             p.lse[static_cast<size_t>(p.sc.head_of(cur.u)) * p.n + qrow] =
                 (m_run[r] + log2f(l_row[r])) * 0.6931471805599453f;
         }
@@ -646,7 +646,7 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
                            kSiteSoftStage))
             return;
           const int r0 = p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
-          if (r0 < p.n) {
+          if (r0 < p.nq) {
             const HeadBatch ob = head_batch(p, cur.u);
 #pragma unroll
             for (int x = 0; x < Cfg::kBoxes; ++x)
@@ -709,7 +709,7 @@ __device__ __forceinline__ void store_role(const FwdParams& p, uint8_t* smem, ui
           break;
         }
         const int r0 = p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows;
-        if (r0 < p.n) {
+        if (r0 < p.nq) {
           const uint32_t stage =
               smem_addr(smem + Cfg::kQOff + (b * Cfg::NQ + tile) * Cfg::kTileBytes);
 #pragma unroll
@@ -813,7 +813,8 @@ struct MergeParams {
   void* out;          // fp16 / bf16, row (b, h, n) at b * stride_b + h * stride_h + n * stride_n
   float* lse;         // optional [BH][N] natural-log log-sum-exp (null: not written)
   const float* workspace;
-  int n;
+  int n;              // rows per head of lse
+  int nq;             // query rows per head in this launch (out starts at the first)
   int heads;
   long long stride_b, stride_h, stride_n;  // in elements
   Schedule sc;
@@ -872,7 +873,7 @@ __global__ void __launch_bounds__(kRowsPerUnit * kMergeThreadsPerRow)
     return i == 0 ? first : mp.workspace + static_cast<size_t>(2 * (c + i)) * kSlotFloats;
   };
   grid_dependency_wait();
-  if (qrow >= mp.n) return;
+  if (qrow >= mp.nq) return;
 
   // Piece 0 holds key block 0, so its row max is finite for every row (causal included) and
   // the running max is finite from the first pair on; a fully masked later piece has

@@ -160,12 +160,14 @@ struct Schedule {
   }
 };
 
-inline Schedule make_schedule(long long bh, long long n, int rows_per_unit, int keys_per_block,
-                              bool causal) {
+// nq query rows and nk keys per head; the causal schedule needs nq == nk (the launcher
+// checks it).
+inline Schedule make_schedule(long long bh, long long nq, long long nk, int rows_per_unit,
+                              int keys_per_block, bool causal) {
   Schedule s;
   s.bh = static_cast<int>(bh);
-  s.q_blocks = static_cast<int>((n + rows_per_unit - 1) / rows_per_unit);
-  s.nkb = static_cast<int>((n + keys_per_block - 1) / keys_per_block);
+  s.q_blocks = static_cast<int>((nq + rows_per_unit - 1) / rows_per_unit);
+  s.nkb = static_cast<int>((nk + keys_per_block - 1) / keys_per_block);
   s.group = rows_per_unit / keys_per_block;
   s.causal = causal ? 1 : 0;
   s.head_steps = causal ? s.pos_first(s.q_blocks - 1) + s.steps_of<true>(s.qb_at(s.q_blocks - 1))

@@ -10,10 +10,11 @@ the calls raise.
 ``forward_lse`` also returns the row log-sum-exp; ``backward`` computes (dq, dk, dv) from it
 (D = 64); ``attention`` is the differentiable forward built from the two.
 ``forward_pinned`` runs the same forward on host tensors, overlapping the host<->device
-copies of batch*head slices with the kernels.
+copies of batch*head slices with the kernels. ``forward_rows`` computes a range of query rows
+of every head (the per-GPU call when fewer batch*head rows than GPUs are sharded by query rows).
 """
 from ._cuda import (attention, backward, forward, forward_bnhd, forward_lse, forward_pinned,
-                    forward_wmma)
+                    forward_rows, forward_wmma)
 
-__all__ = ["forward", "forward_wmma", "forward_bnhd", "forward_pinned", "forward_lse",
-           "backward", "attention"]
+__all__ = ["forward", "forward_wmma", "forward_bnhd", "forward_pinned", "forward_rows",
+           "forward_lse", "backward", "attention"]

@@ -77,6 +77,18 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return _Attention.apply(q, k, v, causal)
 
 
+def forward_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_begin: int, q_end: int,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Non-causal forward of the query rows [q_begin, q_end) of every head, each against all N
+    keys, written into ``out`` (same shape as q; a new tensor if None) and nowhere else: the
+    per-GPU call of the query-row sharding used when B*H is smaller than the number of GPUs
+    (every GPU holds the whole k and v)."""
+    if out is None:
+        out = torch.empty_like(q)
+    _load_extension().forward_rows(q, k, v, out, int(q_begin), int(q_end))
+    return out
+
+
 def forward_bnhd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                  causal: bool = False) -> torch.Tensor:
     """forward on [B, N, H, D] tensors (the flash-attn layout); the output has that layout."""

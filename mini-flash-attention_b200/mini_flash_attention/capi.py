@@ -16,6 +16,7 @@ EXPORTED_SYMBOLS = (
     "mfa_fwd_simple_f16",
     "mfa_fwd_f16_noalloc",
     "mfa_fwd",
+    "mfa_fwd_rows",
     "mfa_fwd_lse",
     "mfa_bwd",
     "mfa_last_error_string",
@@ -64,6 +65,10 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
                                                     ctypes.c_int32, ctypes.c_int32,
                                                     ctypes.c_void_p]
     lib.mfa_fwd.restype = ctypes.c_int
+    lib.mfa_fwd_rows.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 5 + [
+        ctypes.c_int32, ctypes.c_float, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_void_p]
+    lib.mfa_fwd_rows.restype = ctypes.c_int
     lib.mfa_fwd_lse.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64, ctypes.c_int64,
                                                         ctypes.c_int64, ctypes.c_int32,
                                                         ctypes.c_float, ctypes.c_int32,
@@ -122,6 +127,14 @@ def fwd_general(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, he
     """Launch mfa_fwd (dtype and layout selectable); raises MfaError."""
     _check(load().mfa_fwd(q_ptr, k_ptr, v_ptr, out_ptr, batch, heads, n, d, scale, int(causal),
                           dtype, layout, stream))
+
+
+def fwd_rows(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, heads: int,
+             n: int, q_begin: int, q_end: int, d: int, scale: float, causal: bool = False,
+             dtype: int = DTYPE_FP16, layout: int = LAYOUT_BHND, stream: int = 0) -> None:
+    """Launch mfa_fwd_rows (query rows [q_begin, q_end) of every head); raises MfaError."""
+    _check(load().mfa_fwd_rows(q_ptr, k_ptr, v_ptr, out_ptr, batch, heads, n, q_begin, q_end, d,
+                               scale, int(causal), dtype, layout, stream))
 
 
 def bwd(q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, do_ptr: int, lse_ptr: int, dq_ptr: int,

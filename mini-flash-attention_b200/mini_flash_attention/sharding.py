@@ -2,8 +2,10 @@
 
 Every (batch*head) row of the [B*H, N, D] problem is independent, so the path shards by
 contiguous blocks of batch*head rows: rank r owns rows [start, stop) of q, k, v and out, which
-are contiguous slices of memory. Nothing crosses GPUs on the hot path; a caller that wants the
-whole output back gathers the slices outside the timed region.
+are contiguous slices of memory. With fewer batch*head rows than ranks, every query row is
+still independent once a rank holds the whole k and v: the ranks then split the query rows of
+every head instead (`q_shard`, computed by `forward_rows`). Nothing crosses GPUs on the hot
+path; a caller that wants the whole output back gathers the slices outside the timed region.
 
 The reference has no multi-GPU mode; this module only decides who owns what.
 """
@@ -39,3 +41,41 @@ def bh_shard(total_bh: int, rank: int, world: int) -> Shard:
 
 def all_shards(total_bh: int, world: int) -> list[Shard]:
     return [bh_shard(total_bh, r, world) for r in range(world)]
+
+
+# query rows of one forward unit (two 128-row tiles): range boundaries on these keep every
+# unit whole on one rank
+Q_ALIGN = 256
+
+
+@dataclass(frozen=True)
+class QShard:
+    rank: int
+    world: int
+    begin: int  # first query row (of every head) computed by this rank
+    end: int    # one past the last
+
+    @property
+    def rows(self) -> int:
+        return self.end - self.begin
+
+
+def q_shard(n: int, rank: int, world: int, align: int = Q_ALIGN) -> QShard:
+    """Contiguous split of the query rows [0, n) over `world` ranks in blocks of `align` rows
+    (block counts differ by <= 1, the first ranks take the extra blocks; the last block may be
+    short; ranks past the number of blocks get an empty range at n)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank/world {rank}/{world}")
+    if n < 0 or align <= 0:
+        raise ValueError("negative sequence length or bad alignment")
+    blocks = -(-n // align)
+    base, extra = divmod(blocks, world)
+    b0 = rank * base + min(rank, extra)
+    b1 = b0 + base + (1 if rank < extra else 0)
+    return QShard(rank, world, min(b0 * align, n), min(b1 * align, n))
+
+
+def shard_mode(total_bh: int, world: int) -> str:
+    """'rows': batch*head rows per rank (bh_shard); 'queries': query rows of every head per rank
+    (q_shard, the whole k and v on every rank), when there are fewer batch*head rows than ranks."""
+    return "rows" if total_bh >= world else "queries"

@@ -72,3 +72,69 @@ def test_two_rank_gloo_sharded_forward_matches_full():
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) == 0.0
+
+
+# ---- query-row sharding (fewer batch*head rows than ranks)
+from mini_flash_attention.sharding import Q_ALIGN, q_shard, shard_mode  # noqa: E402
+
+
+@pytest.mark.parametrize("n,world", [(65536, 2), (65536, 8), (8192, 3), (1000, 8), (1, 4),
+                                     (257, 2), (0, 2), (4096, 16)])
+def test_query_shards_cover_rows_once_in_whole_units(n, world):
+    shards = [q_shard(n, r, world) for r in range(world)]
+    assert shards[0].begin == 0 and shards[-1].end == n
+    for a, b in zip(shards, shards[1:]):
+        assert a.end == b.begin
+    for s in shards:
+        assert 0 <= s.begin <= s.end <= n
+        assert s.begin % Q_ALIGN == 0 or s.begin == n
+    blocks = [-(-s.rows // Q_ALIGN) for s in shards]
+    assert max(blocks) - min(blocks) <= 1
+
+
+def test_shard_mode_switches_below_one_row_per_rank():
+    assert shard_mode(8, 8) == "rows" and shard_mode(256, 8) == "rows"
+    assert shard_mode(4, 8) == "queries" and shard_mode(1, 2) == "queries"
+
+
+def _q_worker(rank, world, port, result_q):
+    import torch
+    import torch.distributed as dist
+
+    from make_golden import make_inputs
+    from oracle.attention import naive_attention
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    n = 600
+    q, k, v = (x.reshape(1, n, 64) for x in make_inputs((1, 1, n, 64), "normal", 5))
+    assert shard_mode(1, world) == "queries"
+    sh = q_shard(n, rank, world)
+    # every rank holds the whole k and v; its query rows attend to all of them
+    local = naive_attention(q[:, sh.begin:sh.end], k, v)
+    sizes = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(sizes, torch.tensor([sh.rows]))
+    most = max(int(s.item()) for s in sizes)  # gloo gathers equal sizes: pad, then trim
+    padded = torch.zeros((1, most, 64))
+    padded[:, :sh.rows] = torch.from_numpy(np.ascontiguousarray(local)).float()
+    pieces = [torch.zeros((1, most, 64)) for _ in sizes]
+    dist.all_gather(pieces, padded)
+    if rank == 0:
+        full = torch.cat([p[:, :int(s.item())] for p, s in zip(pieces, sizes)], dim=1).numpy()
+        want = naive_attention(q, k, v)
+        result_q.put(float(np.max(np.abs(full - want))))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_gloo_query_sharded_forward_matches_full():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_q_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) == 0.0
