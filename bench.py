@@ -305,7 +305,9 @@ def run_ours(args, wl) -> dict | None:
         bh = global_bh
         qs = q_shard(n, rank, world)
         q_range = (qs.begin, qs.end)
-    inputs = [make_inputs(wl, bh, rank * INPUT_BUFFERS + i, dev, d, dtype, with_grad=train)
+    # query-row sharding: every rank holds the same whole inputs
+    seed0 = (rank if q_range is None else 0) * INPUT_BUFFERS
+    inputs = [make_inputs(wl, bh, seed0 + i, dev, d, dtype, with_grad=train)
               for i in range(INPUT_BUFFERS)]
     flush = torch.empty(L2_FLUSH_MB * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     causal = args.causal
