@@ -300,10 +300,10 @@ def run_ours(args, wl) -> dict | None:
     else:
         # fewer batch*head rows than GPUs: every rank holds the whole q, k, v and computes a
         # range of query rows of every head
-        if train or args.causal:
-            raise SystemExit("query-row sharding (B*H < GPUs) is forward-only and non-causal")
+        if train:
+            raise SystemExit("query-row sharding (B*H < GPUs) is forward-only")
         bh = global_bh
-        qs = q_shard(n, rank, world)
+        qs = q_shard(n, rank, world, causal=args.causal)
         q_range = (qs.begin, qs.end)
     # query-row sharding: every rank holds the same whole inputs
     seed0 = (rank if q_range is None else 0) * INPUT_BUFFERS
@@ -324,7 +324,8 @@ def run_ours(args, wl) -> dict | None:
         rows_out = torch.empty_like(inputs[0][0])
 
         def fwd(q, k, v):
-            return mfa.forward_rows(q, k, v, q_range[0], q_range[1], out=rows_out)
+            return mfa.forward_rows(q, k, v, q_range[0], q_range[1], out=rows_out,
+                                    causal=causal)
 
     stream = torch.cuda.current_stream(dev)
 
@@ -387,8 +388,10 @@ def run_ours(args, wl) -> dict | None:
     # a training step counts the forward (2 products) and the backward (5 products)
     flop_mult = 3.5 if train else 1.0
     flops_rank_step = flop_mult * attention_flops(bh, n, d, causal=causal)
-    if q_range is not None:  # this rank's query rows attend to all n keys
-        flops_rank_step *= (q_range[1] - q_range[0]) / n
+    if q_range is not None:  # this rank's query rows (with the mask: keys up to each row)
+        a, b = q_range
+        flops_rank_step = (4.0 * bh * d * (b * (b + 1) / 2 - a * (a + 1) / 2) if causal
+                           else flops_rank_step * (b - a) / n)
     job_flops_step = flop_mult * attention_flops(global_bh, n, d, causal=causal)
     value = job_flops_step * args.steps / (total_ms / 1e3) / 1e12
     kernel_ms = total_ms / args.steps

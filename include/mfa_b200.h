@@ -87,9 +87,10 @@ MFA_API int mfa_fwd(const void* q, const void* k, const void* v, void* out, int6
  * mfa_fwd restricted to the query rows [q_begin, q_end) of every head: q, k, v and out are the
  * whole tensors (as for mfa_fwd), every query row in the range attends to all N keys, and only
  * those rows of out are written. For multi-GPU sharding when B*H is smaller than the number of
- * GPUs: each GPU holds the whole k and v and takes a range of query rows. Non-causal only
- * (causal != 0 with a range other than [0, N): MFA_ERR_INVALID_ARGUMENT); 0 <= q_begin <=
- * q_end <= N. No counterpart in the reference, which has no multi-GPU mode.
+ * GPUs: each GPU holds the whole k and v and takes a range of query rows. causal != 0 masks
+ * key index > query index as in mfa_fwd (absolute indices); a causal range must start at a
+ * multiple of 256 rows (MFA_ERR_INVALID_ARGUMENT otherwise). 0 <= q_begin <= q_end <= N.
+ * No counterpart in the reference, which has no multi-GPU mode.
  */
 MFA_API int mfa_fwd_rows(const void* q, const void* k, const void* v, void* out, int64_t batch,
                          int64_t heads, int64_t n, int64_t q_begin, int64_t q_end, int32_t d,

@@ -189,9 +189,10 @@ void flash_attn_forward_into(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
 }
 
 // Query rows [q_begin, q_end) of every head of out ([B, H, N, D] or [B*H, N, D], the shape of
-// q), each against all N keys; the other rows of out are left as they are. Non-causal.
+// q), each against all N keys (causal: the keys up to the row); the other rows of out are left
+// as they are. A causal range starts at a multiple of 256 rows.
 void flash_attn_forward_rows(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
-                             int64_t q_begin, int64_t q_end) {
+                             int64_t q_begin, int64_t q_end, bool causal) {
   check_forward_inputs(q, k, v, true, Layout::kBHND);
   TORCH_CHECK(out.is_cuda() && out.device() == q.device(), "out must be on q's device");
   TORCH_CHECK(out.scalar_type() == q.scalar_type(), "out must have q's dtype");
@@ -202,8 +203,8 @@ void flash_attn_forward_rows(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
   const float scale = 1.0f / std::sqrt(static_cast<float>(e.d));
   const int dtype = q.scalar_type() == torch::kBFloat16 ? MFA_DTYPE_BF16 : MFA_DTYPE_FP16;
   const int rc = mfa_fwd_rows(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), e.batch,
-                              e.heads, e.n, q_begin, q_end, static_cast<int32_t>(e.d), scale, 0,
-                              dtype, MFA_LAYOUT_BHND,
+                              e.heads, e.n, q_begin, q_end, static_cast<int32_t>(e.d), scale,
+                              causal ? 1 : 0, dtype, MFA_LAYOUT_BHND,
                               static_cast<void*>(at::cuda::getCurrentCUDAStream().stream()));
   if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
 }
@@ -345,7 +346,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_into", &flash_attn_forward_into,
         "Mini Flash Attention forward into a preallocated output tensor");
   m.def("forward_rows", &flash_attn_forward_rows,
-        "Forward of the query rows [q_begin, q_end) of every head into out (non-causal)");
+        "Forward of the query rows [q_begin, q_end) of every head into out");
   m.def("forward_pinned", &flash_attn_forward_pinned,
         "Pipelined forward on host tensors [rows, N, D] cut into pieces at `bounds`");
   m.def("version", []() { return std::string(mfa_version()); });

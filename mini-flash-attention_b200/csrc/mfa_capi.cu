@@ -251,16 +251,18 @@ struct Plan {
   size_t workspace_bytes = 0;  // split mode: partial-result slots
 };
 
-// nq query rows and n keys per head (nq == n but for a row range).
+// nq query rows and n keys per head (nq == n but for a row range; causal: qb0 query blocks of
+// the head come before the range, and n is one past its last row).
 template <class Cfg>
-int plan_forward(int64_t bh, int64_t nq, int64_t n, int64_t sms, Plan& pl) {
+int plan_forward(int64_t bh, int64_t nq, int64_t n, int64_t sms, Plan& pl, int64_t qb0 = 0) {
   const int64_t q_blocks = (nq + Cfg::kRowsPerUnit - 1) / Cfg::kRowsPerUnit;
   const int64_t nkb = (n + Cfg::kKeys - 1) / Cfg::kKeys;
   const int64_t units = q_blocks * bh;
   if (static_cast<double>(units) * static_cast<double>(nkb) > static_cast<double>(int64_t(1) << 40) ||
       units > 0x7fffffffLL)
     return fail(MFA_ERR_INVALID_ARGUMENT, "B * H * N is too large");
-  pl.sc = make_schedule(bh, nq, n, Cfg::kRowsPerUnit, Cfg::kKeys, Cfg::kCausal);
+  pl.sc = make_schedule(bh, nq, n, Cfg::kRowsPerUnit, Cfg::kKeys, Cfg::kCausal,
+                        static_cast<int>(qb0));
   const int64_t total = pl.sc.total();
   pl.ctas = units < sms ? units : sms;
   pl.split = 0;
@@ -294,7 +296,8 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
   *rc = MFA_OK;
   const bool bf16 = Cfg::kBF16;
   const int64_t d = Cfg::kHeadDim;
-  const int64_t nq = (q_end < 0 ? n : q_end) - q_begin;
+  if (q_end < 0) q_end = n;
+  const int64_t nq = q_end - q_begin;
   const Strides st = layout_strides(layout, heads, n, d);
   const size_t row_off = static_cast<size_t>(q_begin) * static_cast<size_t>(st.n) * 2;  // bytes
   const void* q_rows = static_cast<const char*>(q) + row_off;
@@ -307,8 +310,10 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
     return cudaSuccess;
   if ((*rc = encode_tensor(&p.tm_o, out_rows, batch, heads, n, d, layout, bf16, nq)) != MFA_OK)
     return cudaSuccess;
-  p.n = static_cast<int>(n);
+  // keys: all n, or with the mask the first q_end (later keys are masked for every row)
+  p.n = static_cast<int>(Cfg::kCausal ? q_end : n);
   p.nq = static_cast<int>(nq);
+  p.q0 = static_cast<int>(q_begin);
   p.heads = static_cast<int>(heads);
   p.sc = pl.sc;
   p.split = pl.split;
@@ -347,6 +352,9 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
   const int64_t bh = batch * heads;
   if (q_end < 0) q_end = n;
   if (bh == 0 || n == 0 || q_end == q_begin) return MFA_OK;
+  if (Cfg::kCausal && q_begin % Cfg::kRowsPerUnit != 0)
+    return fail(MFA_ERR_INVALID_ARGUMENT,
+                "a causal query row range must start at a multiple of 256 rows");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
@@ -354,7 +362,8 @@ int launch_forward(const void* q, const void* k, const void* v, void* out, int64
   if (rc != MFA_OK) return rc;
   if ((rc = check_device_pointers(q, k, v, out, dev)) != MFA_OK) return rc;
   Plan pl;
-  if ((rc = plan_forward<Cfg>(bh, q_end - q_begin, n, g_devices[dev].num_sms, pl)) != MFA_OK)
+  if ((rc = plan_forward<Cfg>(bh, q_end - q_begin, Cfg::kCausal ? q_end : n,
+                              g_devices[dev].num_sms, pl, q_begin / Cfg::kRowsPerUnit)) != MFA_OK)
     return rc;
   float* workspace = nullptr;
   if (pl.split) {
@@ -613,8 +622,6 @@ int fwd_general(const void* q, const void* k, const void* v, void* out, float* l
   if (q_end < 0) q_end = n;
   if (q_begin < 0 || q_begin > q_end || q_end > n)
     return fail(MFA_ERR_INVALID_ARGUMENT, "query rows must satisfy 0 <= q_begin <= q_end <= N");
-  if (causal && (q_begin != 0 || q_end != n))
-    return fail(MFA_ERR_INVALID_ARGUMENT, "a query row range needs causal = 0");
   if (lse != nullptr && (q_begin != 0 || q_end != n))
     return fail(MFA_ERR_INVALID_ARGUMENT, "a query row range writes no log-sum-exp");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

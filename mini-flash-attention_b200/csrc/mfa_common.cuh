@@ -20,6 +20,7 @@ struct FwdParams {
   int n;                      // sequence length (keys, and queries of a whole launch)
   int nq;                     // query rows per head in this launch (n, or a row range's length:
                               // tm_q / tm_o then start at the range's first row)
+  int q0;                     // the range's first row (0 for a whole launch): causal mask origin
   int heads;                  // H: a (batch * head) row bh is head bh % H of batch bh / H
   Schedule sc;                // query blocks, key blocks and steps (mfa_schedule.cuh)
   // Persistent schedule. split == 0 (never with causal masking): whole query blocks, CTA c

@@ -583,7 +583,8 @@ __device__ __forceinline__ void softmax_role(const FwdParams& p, uint8_t* smem, 
     float m_run[2] = {-INFINITY, -INFINITY};  // running max of s*scale*log2(e), per row
     float l_run[2] = {0.0f, 0.0f};            // this thread's partial row sums
     const int row0 =  // first query row of this warp's slice (causal masking only)
-        Cfg::kCausal ? p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows + slice : 0;
+        Cfg::kCausal ? p.q0 + p.sc.qb_of(cur.u) * Cfg::kRowsPerUnit + tile * Cfg::kRows + slice
+                     : 0;
     for (int j = cur.j0; j < cur.j1; ++j, ++g) {
       if (!softmax_step<Cfg>(p, bars, tS, tP, tO, tile, lane, g, j, row0, j == cur.j0, m_run,
                              l_run, wd))

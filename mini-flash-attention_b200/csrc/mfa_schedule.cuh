@@ -13,6 +13,9 @@
 // qb = 0, Q-1, 1, Q-2, ... (Q = q_blocks): every pair after the first has group * (Q + 1)
 // steps, so an even split of the steps gives every CTA about the same number of query
 // blocks, i.e. of unit epilogues and diagonal (masked) blocks, and a step is located in O(1).
+// A launch over a range of query rows that starts at query block qb0 of the head (a row range
+// that begins on a unit boundary) numbers its blocks from there: block qb needs
+// group * (qb + 1 + qb0) key blocks, and the pairs keep a constant length.
 #pragma once
 
 #include <cmath>
@@ -44,7 +47,8 @@ struct Schedule {
   int q_blocks;          // query blocks per head: ceil(N / rows_per_unit)
   int nkb;               // key blocks per head: ceil(N / 128)
   int group;             // rows_per_unit / 128
-  int causal;            // 1: query block qb stops at key block group * (qb + 1)
+  int causal;            // 1: query block qb stops at key block group * (qb + 1 + qb0)
+  int qb0;               // causal: query blocks of the head before this launch's first
   long long head_steps;  // steps of one head
   // split mode: CTA c of `ctas` takes the global steps [c * total / ctas, (c+1) * total / ctas),
   // computed as c * cta_q + c * cta_r / ctas with total = cta_q * ctas + cta_r (set_ctas)
@@ -77,7 +81,7 @@ struct Schedule {
   __host__ __device__ int steps_of(int qb) const {
     if (!kCausal) return nkb;
     // only the last query block can reach past key block nkb - 1 (it holds row N - 1)
-    return qb == q_blocks - 1 ? nkb : (qb + 1) * group;
+    return qb == q_blocks - 1 ? nkb : (qb + 1 + qb0) * group;
   }
   // Causal order: query block at position k of its head, and the position of query block qb.
   __host__ __device__ int qb_at(int k) const {
@@ -87,9 +91,11 @@ struct Schedule {
     return 2 * qb < q_blocks ? 2 * qb : 2 * (q_blocks - 1 - qb) + 1;
   }
   // Causal: steps of the first pair (query blocks 0 and Q-1) and of every later pair.
-  __host__ __device__ long long pair0() const { return static_cast<long long>(group) + nkb; }
+  __host__ __device__ long long pair0() const {
+    return static_cast<long long>(group) * (1 + qb0) + nkb;
+  }
   __host__ __device__ long long pair_steps() const {
-    return static_cast<long long>(group) * (q_blocks + 1);
+    return static_cast<long long>(group) * (q_blocks + 1 + 2LL * qb0);
   }
   // Causal: first step (within its head) of the query block at position k.
   __host__ __device__ long long pos_first(int k) const {
@@ -160,12 +166,13 @@ struct Schedule {
   }
 };
 
-// nq query rows and nk keys per head; the causal schedule needs nq == nk (the launcher
-// checks it).
+// nq query rows and nk keys per head. Causal: the rows start at query block qb0 of the head
+// and nk is one past their last row (the keys after it are masked for every row).
 inline Schedule make_schedule(long long bh, long long nq, long long nk, int rows_per_unit,
-                              int keys_per_block, bool causal) {
+                              int keys_per_block, bool causal, int qb0 = 0) {
   Schedule s;
   s.bh = static_cast<int>(bh);
+  s.qb0 = causal ? qb0 : 0;
   s.q_blocks = static_cast<int>((nq + rows_per_unit - 1) / rows_per_unit);
   s.nkb = static_cast<int>((nk + keys_per_block - 1) / keys_per_block);
   s.group = rows_per_unit / keys_per_block;

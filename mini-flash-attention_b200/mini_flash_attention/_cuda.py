@@ -78,14 +78,15 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 def forward_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_begin: int, q_end: int,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """Non-causal forward of the query rows [q_begin, q_end) of every head, each against all N
-    keys, written into ``out`` (same shape as q; a new tensor if None) and nowhere else: the
+                 out: torch.Tensor | None = None, causal: bool = False) -> torch.Tensor:
+    """Forward of the query rows [q_begin, q_end) of every head, each against all N keys (with
+    ``causal``, the keys up to its own index; the range must then start at a multiple of 256
+    rows), written into ``out`` (same shape as q; a new tensor if None) and nowhere else: the
     per-GPU call of the query-row sharding used when B*H is smaller than the number of GPUs
     (every GPU holds the whole k and v)."""
     if out is None:
         out = torch.empty_like(q)
-    _load_extension().forward_rows(q, k, v, out, int(q_begin), int(q_end))
+    _load_extension().forward_rows(q, k, v, out, int(q_begin), int(q_end), bool(causal))
     return out
 
 

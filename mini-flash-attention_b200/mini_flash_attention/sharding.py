@@ -11,6 +11,7 @@ The reference has no multi-GPU mode; this module only decides who owns what.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 
@@ -60,18 +61,26 @@ class QShard:
         return self.end - self.begin
 
 
-def q_shard(n: int, rank: int, world: int, align: int = Q_ALIGN) -> QShard:
+def q_shard(n: int, rank: int, world: int, align: int = Q_ALIGN,
+            causal: bool = False) -> QShard:
     """Contiguous split of the query rows [0, n) over `world` ranks in blocks of `align` rows
-    (block counts differ by <= 1, the first ranks take the extra blocks; the last block may be
-    short; ranks past the number of blocks get an empty range at n)."""
+    (the last block may be short; ranks past the number of blocks get an empty range at n).
+    Without the mask every row costs the same: block counts differ by <= 1, the first ranks
+    take the extra blocks. With it row i attends to i + 1 keys, so rows [0, x) cost about x^2:
+    rank r ends at block round(blocks * sqrt((r + 1) / world))."""
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"bad rank/world {rank}/{world}")
     if n < 0 or align <= 0:
         raise ValueError("negative sequence length or bad alignment")
     blocks = -(-n // align)
-    base, extra = divmod(blocks, world)
-    b0 = rank * base + min(rank, extra)
-    b1 = b0 + base + (1 if rank < extra else 0)
+    if causal:
+        def edge(r: int) -> int:
+            return round(blocks * math.sqrt(r / world))
+        b0, b1 = edge(rank), edge(rank + 1)
+    else:
+        base, extra = divmod(blocks, world)
+        b0 = rank * base + min(rank, extra)
+        b1 = b0 + base + (1 if rank < extra else 0)
     return QShard(rank, world, min(b0 * align, n), min(b1 * align, n))
 
 

@@ -15,18 +15,24 @@ import pytest
 
 
 class Schedule:
-    def __init__(self, bh, n, rows_per_unit, causal, keys=128):
+    """Query rows [q_begin, q_end) of every head (all n by default); with the mask the range
+    starts on a unit boundary, its blocks are numbered from qb0 = q_begin / rows_per_unit and
+    the keys end at q_end (make_schedule's nq, nk, qb0)."""
+
+    def __init__(self, bh, n, rows_per_unit, causal, keys=128, q_begin=0, q_end=None):
+        q_end = n if q_end is None else q_end
         self.bh = bh
-        self.q_blocks = -(-n // rows_per_unit)
-        self.nkb = -(-n // keys)
+        self.q_blocks = -(-(q_end - q_begin) // rows_per_unit)
+        self.nkb = -(-(q_end if causal else n) // keys)
         self.group = rows_per_unit // keys
         self.causal = causal
+        self.qb0 = q_begin // rows_per_unit if causal else 0
         self.head_steps = sum(self.steps_of(qb) for qb in range(self.q_blocks))
 
     def steps_of(self, qb):
         if not self.causal:
             return self.nkb
-        return self.nkb if qb == self.q_blocks - 1 else (qb + 1) * self.group
+        return self.nkb if qb == self.q_blocks - 1 else (qb + 1 + self.qb0) * self.group
 
     # causal processing order within a head: position k holds query block qb_at(k)
     def qb_at(self, k):
@@ -40,8 +46,14 @@ class Schedule:
         return [self.qb_at(k) for k in range(self.q_blocks)] if self.causal \
             else list(range(self.q_blocks))
 
+    def pair0(self):
+        return self.group * (1 + self.qb0) + self.nkb
+
+    def pair(self):
+        return self.group * (self.q_blocks + 1 + 2 * self.qb0)
+
     def pos_first(self, k):
-        pair0, pair = self.group + self.nkb, self.group * (self.q_blocks + 1)
+        pair0, pair = self.pair0(), self.pair()
         m = k // 2
         f = 0 if m == 0 else pair0 + (m - 1) * pair
         return f + (self.steps_of(m) if k % 2 else 0)
@@ -68,7 +80,7 @@ class Schedule:
         if not self.causal:
             return head * self.q_blocks + r // self.nkb, r % self.nkb
         pairs = self.q_blocks // 2
-        pair0, pair = self.group + self.nkb, self.group * (self.q_blocks + 1)
+        pair0, pair = self.pair0(), self.pair()
         if pairs > 0 and r < pair0:
             k, rem = 0, r
         elif pairs > 1 and r < pair0 + (pairs - 1) * pair:
@@ -87,8 +99,8 @@ def split_range(total, cta, ctas):
     return total * cta // ctas, total * (cta + 1) // ctas
 
 
-def plan(bh, n, rows_per_unit, sms, causal):
-    sc = Schedule(bh, n, rows_per_unit, causal)
+def plan(bh, n, rows_per_unit, sms, causal, q_begin=0, q_end=None):
+    sc = Schedule(bh, n, rows_per_unit, causal, q_begin=q_begin, q_end=q_end)
     units = sc.q_blocks * bh
     ctas, split = min(units, sms), 0
     if causal:
@@ -295,3 +307,36 @@ def test_magic_division_by_query_blocks(d):
     for u in us:
         if 0 <= u < 1 << 31:
             assert (u * mul) >> shift == u // d, (u, d)
+
+
+# query row ranges (mfa_fwd_rows): the ranges of sharding.q_shard and a few others
+RANGES = [(1, 8192, 256, 148, 0, 4096), (1, 8192, 256, 148, 4096, 8192),
+          (2, 5000, 256, 37, 2048, 5000), (3, 3000, 256, 148, 768, 1792),
+          (1, 65536, 256, 148, 57344, 65536), (2, 1000, 128, 13, 512, 1000),
+          (1, 640, 256, 148, 512, 640)]
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("bh,n,rows,sms,q0,q1", RANGES)
+def test_row_range_steps_once_and_locate(bh, n, rows, sms, q0, q1, causal):
+    sc, ctas, split = plan(bh, n, rows, sms, causal, q0, q1)
+    seen = set()
+    for c in range(ctas):
+        segs = list(segments(sc, split, c, ctas))
+        assert segs == list(cursor_segments(sc, split, c, ctas))
+        for u, j0, j1, _ in segs:
+            for j in range(j0, j1):
+                assert (u, j) not in seen
+                seen.add((u, j))
+    units = bh * sc.q_blocks
+    assert seen == {(u, j) for u in range(units) for j in range(sc.steps_of(u % sc.q_blocks))}
+    for u in range(units):
+        qb = u % sc.q_blocks
+        last_row = min(q1, q0 + (qb + 1) * rows) - 1  # absolute row of the block's last query
+        want = last_row // 128 + 1 if causal else -(-n // 128)
+        assert sc.steps_of(qb) == want
+    if causal:
+        step = max(1, sc.total() // 3000)
+        for s_ in list(range(0, sc.total(), step)) + [sc.total() - 1]:
+            u, j = sc.locate(s_)
+            assert sc.unit_first(u) + j == s_

@@ -92,6 +92,20 @@ def test_query_shards_cover_rows_once_in_whole_units(n, world):
     assert max(blocks) - min(blocks) <= 1
 
 
+@pytest.mark.parametrize("n,world", [(65536, 2), (65536, 8), (8192, 3), (5000, 8), (300, 4)])
+def test_causal_query_shards_cover_rows_and_balance_work(n, world):
+    shards = [q_shard(n, r, world, causal=True) for r in range(world)]
+    assert shards[0].begin == 0 and shards[-1].end == n
+    for a, b in zip(shards, shards[1:]):
+        assert a.end == b.begin
+    work = [s.end * (s.end + 1) / 2 - s.begin * (s.begin + 1) / 2 for s in shards]
+    if n >= 256 * 4 * world:  # enough units to balance
+        assert max(work) <= 1.25 * sum(work) / world
+        equal = [q_shard(n, r, world) for r in range(world)]
+        equal_work = [s.end * (s.end + 1) / 2 - s.begin * (s.begin + 1) / 2 for s in equal]
+        assert max(work) < max(equal_work)
+
+
 def test_shard_mode_switches_below_one_row_per_rank():
     assert shard_mode(8, 8) == "rows" and shard_mode(256, 8) == "rows"
     assert shard_mode(4, 8) == "queries" and shard_mode(1, 2) == "queries"
