@@ -246,6 +246,15 @@ def test_forward_pinned_matches_forward(chunks):
     torch.testing.assert_close(out, want, atol=1e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("chunks", [4, 8])
+def test_forward_pinned_causal_ragged(chunks):
+    q, k, v = (randn_cuda((1, 8, 1000, 64), 95 + i) for i in range(3))
+    want = mfa.forward(q, k, v, causal=True).cpu()
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    got = mfa.forward_pinned(hq, hk, hv, causal=True, chunks=chunks)
+    torch.testing.assert_close(got, want, atol=1e-3, rtol=1e-3)
+
+
 def test_forward_pinned_rejects_device_tensors():
     q = torch.zeros(1, 1, 128, 64, device="cuda", dtype=torch.float16)
     with pytest.raises(RuntimeError, match="host tensors"):
