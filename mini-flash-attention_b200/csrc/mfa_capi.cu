@@ -322,9 +322,22 @@ cudaError_t launch_planned(const void* q, const void* k, const void* v, void* ou
   p.status = status_ptr;
   p.workspace = workspace;
   p.lse = lse;
-  mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim, Cfg::kLSE>
-      <<<static_cast<unsigned>(pl.ctas), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  // a programmatic dependent of the stream's previous kernel: its set-up overlaps that
+  // kernel's tail, its memory accesses wait for its completion (griddepcontrol.wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.ctas));
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(
+      &cfg, mfa_fwd_kernel<Cfg::NQ, Cfg::STAGES, Cfg::kCausal, Cfg::kBF16, Cfg::kHeadDim, Cfg::kLSE>,
+      p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e == cudaSuccess && pl.split) {
     MergeParams mp;
     mp.out = out_rows;

@@ -748,6 +748,10 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
   // The split-mode merge kernel may be scheduled now; it waits for this grid to complete
   // before reading anything this grid writes.
   if (threadIdx.x == 0) grid_dependents_launch();
+  // This grid is itself launched as a programmatic dependent of the stream's previous kernel:
+  // the set-up below (barriers, TMEM) may overlap that kernel's tail; every warp then waits
+  // for that kernel's completion before its role starts, i.e. before any global memory
+  // access and before any bounded wait (whose limit would otherwise run during that kernel).
   // The load thread initialises the barriers and goes straight on to its first copies; the
   // other warps wait on named barrier 1 for the barriers and for warp 0's TMEM allocation
   // (the load warp only arrives there), so the first Q/K/V loads leave while TMEM is set up.
@@ -779,6 +783,7 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
     named_bar_arrive(1, Cfg::kThreads);
     if constexpr (Cfg::kRebalanceRegs) setmaxnreg_dec<Cfg::kControlRegs>();
     const Watchdog wd{abort_flag, p.status, p.timeout_ns};
+    grid_dependency_wait();
     if (lane == 0) load_role<Cfg>(p, smem, bars, wd);
   } else {
     if (warp == 0) {
@@ -789,6 +794,7 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
     named_bar_sync(1, Cfg::kThreads);
     tc_fence_after();
     tmem = *tmem_slot;
+    grid_dependency_wait();
     const Watchdog wd{abort_flag, p.status, p.timeout_ns};
     if (warp < Cfg::kSoftmaxWarps) {
       if constexpr (Cfg::kRebalanceRegs) setmaxnreg_inc<Cfg::kSoftmaxRegs>();
