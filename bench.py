@@ -20,6 +20,20 @@ Multi-GPU (torchrun, one rank per GPU): every rank owns a contiguous block of ba
 workload each rank owns its own B=1, H=8 slice (weak scaling: the global batch grows with N);
 for the others the global B*H is split over the ranks (strong scaling).
 
+Besides `value` (whole-job TFLOPS over all ranks; `tflops_per_gpu` = value / n_gpus) the line
+carries, for the default forward:
+  kernel_only     CUDA events around the C-ABI call mfa_fwd_f16 (no torch allocation or
+                  binding), same buffers, flush and steps: the kernels alone;
+  kernel_us       per-kernel device durations of three flushed calls from a CUPTI trace;
+  strong          the strong splits of B16 H16 N4096 (256 batch*head rows contiguous over the
+                  ranks) and B1 H32 N32768 (its 32 heads over the ranks), timed in the same
+                  process after the headline, max over ranks;
+  reference_kernel (one GPU) a GPU baseline leg: the reference's own CuTe kernel (compiled from
+                  its sources into oracle/_ref) on the same buffers, flush and events, timed
+                  after everything else, like cpu_baseline;
+  e2e.copy_gbs    host<->device bytes of one rank's step / that rank's e2e time per step.
+--no-extras leaves all of these out (for profiler runs).
+
 --impl reference times the reference's CPU path (the naive torch attention of
 benchs/benchmark_forward.py:98-115) on this host's cores, one head of the workload per step,
 on rank 0 only; --impl reference --ref-kernel cute times the reference's own CuTe kernel
@@ -250,6 +264,96 @@ def launches_per_call(fn, *args) -> tuple[int | None, list[str]]:
         return None, [f"launch count unavailable: {type(exc).__name__}: {exc}"]
 
 
+def kernel_durations(fn, inputs, flush, calls: int = 3) -> dict:
+    """Median device duration (us) per kernel of this library over `calls` flushed calls, from
+    a CUDA activity trace (torch.profiler over CUPTI)."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for i in range(calls):
+                flush.fill_(1.0)
+                fn(*inputs[i % len(inputs)])
+            torch.cuda.synchronize()
+        per: dict[str, list[float]] = {}
+        for e in prof.events():
+            if e.device_type == torch.autograd.DeviceType.CUDA and "mfa_" in e.name:
+                per.setdefault(e.name, []).append(e.device_time)
+        return {name: round(statistics.median(v), 2) for name, v in sorted(per.items())}
+    except Exception as exc:  # profiler unavailable
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+
+
+def time_calls(fn, inputs, flush, stream, steps: int, warmup: int) -> list[float]:
+    """CUDA-event milliseconds of `steps` calls of fn, a 256 MB L2 flush before each (outside
+    the events), after `warmup` untimed calls."""
+    for i in range(warmup):
+        flush.fill_(1.0)
+        fn(*inputs[i % len(inputs)])
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush.fill_(1.0)
+        starts[i].record(stream)
+        fn(*inputs[i % len(inputs)])
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+
+# strong splits measured after the headline: (workload, warm-up calls, timed calls)
+STRONG = (("b16h16n4096", 3, 10), ("b1h32n32768", 3, 5))
+
+
+def strong_splits(rank: int, world: int, dev, flush, stream) -> dict:
+    """B16 H16 N4096 and B1 H32 N32768 with their global batch*head rows split contiguously
+    over the ranks (no collective on the data path); whole-job TFLOPS from the max over ranks."""
+    import mini_flash_attention as mfa
+    from mini_flash_attention.sharding import bh_shard
+
+    out = {}
+    for name, warmup, steps in STRONG:
+        wl = WORKLOADS[name]
+        global_bh = wl["B"] * wl["H"]
+        sh = bh_shard(global_bh, rank, world)
+        inputs = [make_inputs(wl, sh.rows, 100 + 2 * rank + i, dev) for i in range(2)]
+        ms = time_calls(lambda q, k, v: mfa.forward(q, k, v), inputs, flush, stream, steps,
+                        warmup)
+        barrier(world)
+        step_ms = max_over_ranks(sum(ms) / steps, world)
+        job = attention_flops(global_bh, wl["N"])
+        out[name] = {"ms_per_step": round(step_ms, 4),
+                     "value": round(job / (step_ms / 1e3) / 1e12, 3), "unit": UNIT,
+                     "bh_per_gpu": sh.rows, "global_bh": global_bh, "steps": steps,
+                     "warmup": warmup,
+                     "split": f"{global_bh} batch*head rows contiguous over {world} GPU(s)"}
+        del inputs
+    return out
+
+
+def reference_kernel_leg(wl: dict, inputs, flush, stream, steps: int, warmup: int) -> dict:
+    """GPU baseline leg: the reference's CuTe kernel (src/mini_flash_attention/flash_attn_cuda.cu:
+    190-420, built from its sources into oracle/_ref) on the same buffers, flush and events."""
+    try:
+        from oracle import ref
+
+        if not ref.available():
+            return {"value": None, "reason": f"{ref.LIB_PATH.name} not built"}
+        ms = time_calls(lambda q, k, v: ref.reference_forward(q, k, v, kernel="cute"), inputs,
+                        flush, stream, steps, warmup)
+    except Exception as exc:  # noqa: BLE001  (a baseline must not break the bench line)
+        return {"value": None, "reason": f"{type(exc).__name__}: {exc}"}
+    bh, n = inputs[0][0].shape[0], inputs[0][0].shape[1]
+    t = sum(ms) / steps
+    return {"value": round(attention_flops(bh, n) / (t / 1e3) / 1e12, 3), "unit": UNIT,
+            "ms_per_step": round(t, 4), "median_ms": round(statistics.median(ms), 4),
+            "steps": steps, "warmup": warmup,
+            "kernel": "FlashAttnCuteKernel, reference sources compiled for sm_100a; its binding's "
+                      "zeros_like output inside the timed call (flash_attn.cpp:86)"}
+
+
 # ---------------------------------------------------------------- arms
 def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -360,7 +464,7 @@ def run_ours(args, wl) -> dict | None:
         # ---- end to end: pinned host q, k, v -> device -> forward -> pinned host output,
         # through the public host-buffer API (copies of batch*head slices overlap kernels)
         e2e_steps = max(args.steps, 3)
-        e2e_ms = None
+        e2e_ms = e2e_ms_rank = None
         if not train and q_range is None:
             host_in = [x.cpu().pin_memory() for x in inputs[0]]
             host_out = torch.empty(inputs[0][0].shape, dtype=dtype).pin_memory()
@@ -375,8 +479,41 @@ def run_ours(args, wl) -> dict | None:
             for _ in range(e2e_steps):
                 mfa.forward_pinned(*host_in, causal=causal, out=host_out, chunks=chunks,
                                    device=dev)
-            e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+            e2e_ms_rank = (time.perf_counter() - t0) * 1e3
+            e2e_ms = max_over_ranks(e2e_ms_rank, world)
             barrier(world)
+
+        # ---- extras (outside every timed region above; every rank takes the same collective
+        # steps): kernels alone through the C ABI, per-kernel durations, strong splits
+        extras = {}
+        default_fwd = (not train and q_range is None and d == D and dtype == torch.float16)
+        if default_fwd and not args.no_extras:
+            from mini_flash_attention import capi
+
+            scale = D ** -0.5
+            sid = stream.cuda_stream
+            outs = [torch.empty_like(x[0]) for x in inputs]
+            slot = {"i": 0}
+
+            def capi_fwd(q, k, v):
+                o = outs[slot["i"] % INPUT_BUFFERS]
+                slot["i"] += 1
+                capi.fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), bh, n, D,
+                         scale, causal=causal, stream=sid)
+
+            ms_k = time_calls(capi_fwd, inputs, flush, stream, args.steps, args.warmup)
+            k_ms = max_over_ranks(sum(ms_k) / args.steps, world)
+            extras["kernel_only"] = {
+                "value": round(attention_flops(global_bh, n, d, causal) / (k_ms / 1e3) / 1e12, 3),
+                "unit": UNIT, "ms_per_step": round(k_ms, 4),
+                "timing": "CUDA events around the C-ABI call mfa_fwd_f16, same buffers, flush "
+                          "and step count as value, max over ranks"}
+            extras["kernel_us"] = kernel_durations(fwd, inputs, flush)
+            if not causal:
+                extras["strong"] = strong_splits(rank, world, dev, flush, stream)
+            if world == 1:
+                extras["reference_kernel"] = reference_kernel_leg(
+                    wl, inputs, flush, stream, max(3, min(args.steps, 20)), 3)
 
     if world > 1:
         import torch.distributed as dist
@@ -429,6 +566,8 @@ def run_ours(args, wl) -> dict | None:
             "input_buffers": INPUT_BUFFERS,
             "timing": "CUDA events around each forward() call on its stream, max over ranks",
         },
+        "value_scope": "whole job: TFLOPS summed over all n_gpus ranks (per GPU: "
+                       "tflops_per_gpu); the metric's per-GPU figure is value / n_gpus",
         "tflops_per_gpu": round(value / world, 3),
         "pct_dense_fp16_peak": round(100.0 * achieved / peak, 2),
         "roofline": {
@@ -447,12 +586,17 @@ def run_ours(args, wl) -> dict | None:
         "e2e": ({
             "value": round(e2e_value, 3), "unit": UNIT,
             "h2d_bytes_per_step": bytes_in, "d2h_bytes_per_step": bytes_out,
+            "copy_gbs_per_rank": round(4 * bh * n * d * 2 / (e2e_ms_rank / e2e_steps / 1e3) / 1e9,
+                                       2),
+            "copy_gbs_note": "one rank's host<->device bytes per step (q, k, v in, out back) / "
+                             "that rank's e2e time per step: the e2e limiter is this copy rate",
             "path": "mini_flash_attention.forward_pinned: pinned host q,k,v -> H2D / forward / "
                     "D2H of batch*head slices pipelined on 3 streams -> pinned host out",
             "timing": "host wall clock around the synchronous calls, max over ranks",
         } if e2e_value is not None else {"value": None, "reason": (
             "no host-buffer training API" if train else
             "forward_pinned has no query-row range")}),
+        **extras,
         "gpu_launches": None if per_call is None else per_call * args.steps,
         "gpu_kernels": kernel_names,
         "clocks": clocks,
@@ -552,6 +696,8 @@ def main():
                     help="mask key > query (flops counted over the N(N+1)/2 attended pairs)")
     ap.add_argument("--no-launch-count", action="store_true",
                     help="skip the CUPTI trace that counts launches (for runs under ncu)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip kernel_only, kernel_us, strong and reference_kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -145,7 +145,13 @@ MFA_API int mfa_bwd(const void* q, const void* k, const void* v, const void* out
  *     results. Serialise them, e.g. by issuing them on one stream.
  *   - The first call on each device runs its one-time set-up (device checks, kernel
  *     attributes, cudaGetSymbolAddress of the scratch); make that first call before any
- *     stream capture.
+ *     stream capture. If the set-up fails with a CUDA error, the call returns MFA_ERR_CUDA
+ *     and the next call tries the set-up again; only a device of the wrong architecture
+ *     fails every call.
+ *   - Memory cost to every user of the library: the array belongs to the library's device
+ *     image, so each device on which any kernel of this library is loaded holds
+ *     MFA_NOALLOC_SCRATCH_BYTES for it until the process exits, whether or not this entry
+ *     point is ever called.
  */
 MFA_API int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, void* out, int64_t bh,
                         int64_t n, int32_t d, float scale, int32_t causal, void* stream);

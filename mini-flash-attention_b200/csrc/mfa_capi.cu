@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -130,27 +131,34 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(std::string* why) {
   return fn;
 }
 
+// Architecture check shared by the set-up of every entry point: device `dev` must be an
+// sm_100 GPU. Returns MFA_OK with its SM count, MFA_ERR_DEVICE (a permanent condition) or
+// MFA_ERR_CUDA, with the message in *msg.
+int check_architecture(int dev, int* num_sms, std::string* msg) {
+  int major = 0, minor = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (e == cudaSuccess && (major != 10 || minor != 0)) {
+    *msg = "mini_flash_attention_b200 kernels are built for sm_100a only; device " +
+           std::to_string(dev) + " is sm_" + std::to_string(major) + std::to_string(minor);
+    return MFA_ERR_DEVICE;
+  }
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(num_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) {
+    *msg = std::string("CUDA error: ") + cudaGetErrorString(e);
+    return MFA_ERR_CUDA;
+  }
+  return MFA_OK;
+}
+
 // One-time per-device set-up: architecture check, kernel attributes, status word address.
 int prepare_device(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return fail(MFA_ERR_DEVICE, "device index out of range");
   DeviceState& ds = g_devices[dev];
   std::call_once(ds.once, [&ds, dev] {
-    int major = 0, minor = 0;
-    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
-    if (e != cudaSuccess) {
-      ds.error = MFA_ERR_CUDA;
-      ds.message = std::string("CUDA error: ") + cudaGetErrorString(e);
-      return;
-    }
-    if (major != 10 || minor != 0) {
-      ds.error = MFA_ERR_DEVICE;
-      ds.message = "mini_flash_attention_b200 kernels are built for sm_100a only; device " +
-                   std::to_string(dev) + " is sm_" + std::to_string(major) + std::to_string(minor);
-      return;
-    }
-    e = cudaDeviceGetAttribute(&ds.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = set_smem_attributes_d<32>();
+    ds.error = check_architecture(dev, &ds.num_sms, &ds.message);
+    if (ds.error != MFA_OK) return;
+    cudaError_t e = set_smem_attributes_d<32>();
     if (e == cudaSuccess) e = set_smem_attributes_d<64>();
     if (e == cudaSuccess) e = set_smem_attributes_d<128>();
     if (e == cudaSuccess) e = set_bwd_attributes();
@@ -444,8 +452,9 @@ namespace mfa {
 namespace {
 
 struct NoAllocState {
-  std::once_flag once;
-  int error = MFA_OK;
+  std::mutex mu;                  // serialises the set-up
+  std::atomic<bool> ready{false};  // set-up completed: the fields below are valid
+  int error = MFA_OK;             // a permanent failure (wrong architecture), reported by every call
   std::string message;
   int* status_ptr = nullptr;
   float* scratch = nullptr;
@@ -453,35 +462,39 @@ struct NoAllocState {
 };
 NoAllocState g_noalloc[kMaxDevices];
 
-// One-time per-device set-up of the allocation-free entry point, run with `dev` current: the
-// architecture check and kernel attribute of prepare_device, plus the device addresses of the
-// status word and of the static scratch. It creates no memory pool and allocates nothing.
+// Per-device set-up of the allocation-free entry point, run with `dev` current: the
+// architecture check and kernel attributes of prepare_device, plus the device addresses of
+// the status word and of the static scratch. It creates no memory pool and allocates nothing.
+// Only a wrong architecture is remembered; after any other failure (a CUDA error, e.g. a first
+// call made during stream capture) the set-up runs again on the next call.
 int prepare_noalloc(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return fail(MFA_ERR_DEVICE, "device index out of range");
   NoAllocState& st = g_noalloc[dev];
-  std::call_once(st.once, [&st, dev] {
-    int major = 0, minor = 0;
-    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
-    if (e == cudaSuccess && (major != 10 || minor != 0)) {
-      st.error = MFA_ERR_DEVICE;
-      st.message = "mini_flash_attention_b200 kernels are built for sm_100a only; device " +
-                   std::to_string(dev) + " is sm_" + std::to_string(major) + std::to_string(minor);
-      return;
-    }
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = set_smem_attribute<Full<false, false>>();
-    if (e == cudaSuccess) e = set_smem_attribute<Full<true, false>>();
-    if (e == cudaSuccess)
-      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status_ptr), g_device_status);
-    if (e == cudaSuccess)
-      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.scratch), g_noalloc_scratch);
-    if (e != cudaSuccess) {
-      st.error = MFA_ERR_CUDA;
-      st.message = std::string("CUDA error: ") + cudaGetErrorString(e) + " (no-alloc set-up)";
-    }
-  });
+  if (st.ready.load(std::memory_order_acquire)) return MFA_OK;
+  std::lock_guard<std::mutex> lock(st.mu);
+  if (st.ready.load(std::memory_order_relaxed)) return MFA_OK;
   if (st.error != MFA_OK) return fail(st.error, st.message);
+  std::string msg;
+  int num_sms = 0;
+  const int rc = check_architecture(dev, &num_sms, &msg);
+  if (rc == MFA_ERR_DEVICE) {
+    st.error = rc;
+    st.message = msg;
+  }
+  if (rc != MFA_OK) return fail(rc, msg);
+  int* status_ptr = nullptr;
+  float* scratch = nullptr;
+  cudaError_t e = set_smem_attribute<Full<false, false>>();
+  if (e == cudaSuccess) e = set_smem_attribute<Full<true, false>>();
+  if (e == cudaSuccess)
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status_ptr), g_device_status);
+  if (e == cudaSuccess)
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&scratch), g_noalloc_scratch);
+  if (e != cudaSuccess) return fail_cuda(e, "no-alloc set-up");
+  st.num_sms = num_sms;
+  st.status_ptr = status_ptr;
+  st.scratch = scratch;
+  st.ready.store(true, std::memory_order_release);
   return MFA_OK;
 }
 

@@ -1,7 +1,7 @@
 """ctypes view of the C ABI in include/mfa_b200.h (libmfa_b200.so).
 
-This is the boundary a non-Python host binds; the tests use it to call
-the kernels exactly as such a host would: raw device pointers, sizes and a stream handle.
+This is the boundary a non-Python host binds; the tests use it to call the kernels exactly
+as such a host would: raw device pointers, sizes and a stream handle.
 """
 from __future__ import annotations
 

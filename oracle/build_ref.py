@@ -12,9 +12,10 @@ flashinfer wheel of this image (only stable CuTe APIs are used by the kernel,
 flash_attn_cuda.cu:5-12). The WMMA unit defines its launcher under the CuTe launcher's name
 (flash_attn_wmma_cuda.cu:253), so it is renamed with a -D define at compile time.
 
-Needs the reference checkout (default /root/reference, or $MFA_REFERENCE_ROOT); the built
+The reference checkout is taken from --reference-root, else $MFA_REFERENCE_ROOT, else a
+directory named `reference` beside this repository; without one nothing is built. The built
 library travels with the tree, the sources are never copied into it.
-Usage: python oracle/build_ref.py [--force]
+Usage: python oracle/build_ref.py [--force] [--reference-root DIR]
 """
 from __future__ import annotations
 
@@ -28,8 +29,13 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 OUT_LIB = OUT_DIR / "libmfa_ref.so"
-REFERENCE_ROOT = Path(os.environ.get("MFA_REFERENCE_ROOT", "/root/reference"))
-REF_SRC = REFERENCE_ROOT / "src" / "mini_flash_attention"
+
+
+def reference_sources(root: str | os.PathLike | None = None) -> Path:
+    """src/mini_flash_attention of the reference checkout (see the module docstring)."""
+    if root is None:
+        root = os.environ.get("MFA_REFERENCE_ROOT") or HERE.parent.parent / "reference"
+    return Path(root) / "src" / "mini_flash_attention"
 
 
 def cutlass_include() -> Path:
@@ -48,15 +54,16 @@ def cutlass_include() -> Path:
     raise RuntimeError("no CuTe headers found (set MFA_CUTLASS_INCLUDE)")
 
 
-def available() -> bool:
-    return (REF_SRC / "flash_attn_cuda.cu").exists()
+def available(root: str | os.PathLike | None = None) -> bool:
+    return (reference_sources(root) / "flash_attn_cuda.cu").exists()
 
 
-def build(force: bool = False) -> Path | None:
-    if not available():
+def build(force: bool = False, reference_root: str | os.PathLike | None = None) -> Path | None:
+    if not available(reference_root):
         return None
-    srcs = [REF_SRC / "flash_attn_cuda.cu", REF_SRC / "flash_attn_wmma_cuda.cu",
-            REF_SRC / "utils.cuh", HERE / "ref_shim.cu", Path(__file__)]
+    ref_src = reference_sources(reference_root)
+    srcs = [ref_src / "flash_attn_cuda.cu", ref_src / "flash_attn_wmma_cuda.cu",
+            ref_src / "utils.cuh", HERE / "ref_shim.cu", Path(__file__)]
     if (not force and OUT_LIB.exists()
             and all(s.stat().st_mtime <= OUT_LIB.stat().st_mtime for s in srcs)):
         return OUT_LIB
@@ -64,11 +71,11 @@ def build(force: bool = False) -> Path | None:
     OUT_DIR.mkdir(exist_ok=True)
     inc = cutlass_include()
     common = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "--use_fast_math",
-              "-std=c++17", "-Xcompiler", "-fPIC", f"-I{inc}", f"-I{REF_SRC}"]
+              "-std=c++17", "-Xcompiler", "-fPIC", f"-I{inc}", f"-I{ref_src}"]
     objs = []
     units = [
-        (REF_SRC / "flash_attn_cuda.cu", []),
-        (REF_SRC / "flash_attn_wmma_cuda.cu",
+        (ref_src / "flash_attn_cuda.cu", []),
+        (ref_src / "flash_attn_wmma_cuda.cu",
          ["-Dlaunch_flash_attn_forward=launch_flash_attn_forward_wmma"]),
         (HERE / "ref_shim.cu", []),
     ]
@@ -92,5 +99,7 @@ def build(force: bool = False) -> Path | None:
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--reference-root", default=None)
     a = ap.parse_args()
-    print(build(force=a.force) or "reference sources not present; nothing built")
+    print(build(force=a.force, reference_root=a.reference_root)
+          or "reference sources not present; nothing built")

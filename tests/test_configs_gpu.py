@@ -1,0 +1,124 @@
+"""Whole-output parity on the five workload configurations, against the reference's own CuTe
+kernel run live and against fp32 attention.
+
+Configurations (fp16 q, k, v of layout [B*H, N, 64], non-causal, scale 1/8):
+  C1 [8, 1024, 64]    N(0,1)            the reference's CPU-runnable case
+  C2 [8, 8192, 64]    N(0,1)            the headline benchmark shape
+  C3 [256, 4096, 64]  N(0,1)            throughput shape
+  C4 [32, 32768, 64]  q, k ~ N(0,3^2), v ~ N(0,1): near one-hot softmax rows
+  C5 [2048, 512, 64]  uniform[-1, 1]    short sequences, many heads
+Inputs are drawn on the GPU from one seeded generator per configuration, q, k, v in that order.
+
+Oracles and tolerances:
+  * the reference kernel (src/mini_flash_attention/flash_attn_cuda.cu:190-420, compiled from
+    its sources into oracle/_ref by oracle/build_ref.py): every output element within
+    atol 2e-3 / rtol 1e-2 (the reference test's comparison pattern, tests/test_forward.py:19-38,
+    with the tighter north-star tolerance);
+  * fp32 attention softmax(q k^T / 8) v computed on the GPU in chunks (tests/test_forward.py:
+    28-34), compared unrounded with our fp16 output upcast. Rule: |ours - fp32| <= 1e-3 where
+    |fp32| <= 2; where |fp32| > 2 the fp16 rounding of the output alone reaches |o| * 2^-11
+    (up to 1e-3 at |o| = 4), so there the bound is 1e-3 + 1e-3 * |fp32|.
+The test fails (it does not skip) when the reference build is missing on a GPU machine.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import mini_flash_attention as mfa
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = {
+    # name: (shape, distribution, q/k scale)
+    "C1_b1h8n1024": ((8, 1024, 64), "normal", 1.0),
+    "C2_b1h8n8192": ((8, 8192, 64), "normal", 1.0),
+    "C3_b16h16n4096": ((256, 4096, 64), "normal", 1.0),
+    "C4_b1h32n32768_peaky": ((32, 32768, 64), "normal", 3.0),
+    "C5_b128h16n512_uniform": ((2048, 512, 64), "uniform", 1.0),
+}
+ATOL_REF, RTOL_REF = 2e-3, 1e-2
+ATOL_FP32, RTOL_FP32_ABOVE_2 = 1e-3, 1e-3
+SCORE_BYTES_PER_CHUNK = 1 << 30  # fp32 score block of the chunked oracle
+
+
+def make_inputs(shape, dist, qk_scale, seed=0):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    if dist == "uniform":
+        q, k, v = (torch.rand(shape, device="cuda", generator=g) * 2 - 1 for _ in range(3))
+    else:
+        q, k, v = (torch.randn(shape, device="cuda", generator=g) for _ in range(3))
+        q, k = q * qk_scale, k * qk_scale
+    return q.half().contiguous(), k.half().contiguous(), v.half().contiguous()
+
+
+def naive_fp32_chunked(q, k, v):
+    """fp32 softmax(q k^T D^-0.5) v, heads and query rows in chunks of at most 1 GiB of scores."""
+    bh, n, d = q.shape
+    out = torch.empty(q.shape, device=q.device, dtype=torch.float32)
+    rows = max(1, min(n, SCORE_BYTES_PER_CHUNK // (4 * n)))
+    heads = max(1, min(bh, SCORE_BYTES_PER_CHUNK // (4 * n * rows)))
+    for h0 in range(0, bh, heads):
+        kh = k[h0:h0 + heads].float()
+        vh = v[h0:h0 + heads].float()
+        for r0 in range(0, n, rows):
+            s = q[h0:h0 + heads, r0:r0 + rows].float() @ kh.transpose(-2, -1) * d ** -0.5
+            out[h0:h0 + heads, r0:r0 + rows] = torch.softmax(s, dim=-1) @ vh
+    return out
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _exact_fp32_matmul():
+    # the oracle's products must be full fp32 (no TF32)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def test_reference_build_is_present():
+    assert ref.available(), (f"{ref.LIB_PATH} is missing: build it with oracle/build_ref.py "
+                             "next to a reference checkout before running the GPU tests")
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_whole_output_matches_reference_kernel_and_fp32(name):
+    assert ref.available(), f"{ref.LIB_PATH} is missing"
+    shape, dist, qk_scale = CONFIGS[name]
+    q, k, v = make_inputs(shape, dist, qk_scale)
+    ours = mfa.forward(q, k, v)
+    theirs = ref.reference_forward(q, k, v, kernel="cute")
+    torch.cuda.synchronize()
+    assert torch.isfinite(ours).all() and torch.isfinite(theirs).all()
+
+    diff_ref = (ours.float() - theirs.float()).abs()
+    exact = naive_fp32_chunked(q, k, v)
+    err = (ours.float() - exact).abs()
+    big = exact.abs() > 2
+    bound = torch.where(big, ATOL_FP32 + RTOL_FP32_ABOVE_2 * exact.abs(),
+                        torch.full_like(exact, ATOL_FP32))
+    err_theirs = (theirs.float() - exact).abs()
+    # the figures for the record (pytest -s), the reference kernel against the same oracle too
+    print(f"\n{name}: max|ours-ref|={diff_ref.max().item():.3e} "
+          f"max|ours-fp32|={err.max().item():.3e} (|o|<=2: {err[~big].max().item():.3e}) "
+          f"max|ref-fp32|={err_theirs.max().item():.3e} max|o|={exact.abs().max().item():.3f}")
+
+    torch.testing.assert_close(ours, theirs, atol=ATOL_REF, rtol=RTOL_REF)
+    worst = int((err - bound).argmax())
+    assert bool((err <= bound).all()), (
+        f"{name}: |ours - fp32| = {err.flatten()[worst].item():.3e} at flat index {worst} "
+        f"(fp32 value {exact.flatten()[worst].item():.4f}) exceeds its bound")
+
+
+@pytest.mark.parametrize("name", ["C1_b1h8n1024", "C5_b128h16n512_uniform"])
+def test_forward_wmma_matches_reference_wmma_kernel(name):
+    """forward_wmma (the single-tile kernel) against the reference's WMMA kernel
+    (src/mini_flash_attention/flash_attn_wmma_cuda.cu:34-289), whole output."""
+    assert ref.available(), f"{ref.LIB_PATH} is missing"
+    shape, dist, qk_scale = CONFIGS[name]
+    q, k, v = make_inputs(shape, dist, qk_scale, seed=1)
+    ours = mfa.forward_wmma(q, k, v)
+    theirs = ref.reference_forward(q, k, v, kernel="wmma")
+    torch.testing.assert_close(ours, theirs, atol=ATOL_REF, rtol=RTOL_REF)
