@@ -15,9 +15,13 @@ Oracles and tolerances:
     atol 2e-3 / rtol 1e-2 (the reference test's comparison pattern, tests/test_forward.py:19-38,
     with the tighter north-star tolerance);
   * fp32 attention softmax(q k^T / 8) v computed on the GPU in chunks (tests/test_forward.py:
-    28-34), compared unrounded with our fp16 output upcast. Rule: |ours - fp32| <= 1e-3 where
-    |fp32| <= 2; where |fp32| > 2 the fp16 rounding of the output alone reaches |o| * 2^-11
-    (up to 1e-3 at |o| = 4), so there the bound is 1e-3 + 1e-3 * |fp32|.
+    28-34), compared unrounded with our fp16 output upcast. Rule: |ours - fp32| <= 1e-3 +
+    1e-3 * |fp32| for every element (atol 1e-3 with an rtol of 1e-3 added). The rtol covers
+    two roundings that scale with |o|: the fp16 output (up to |o| * 2^-11) and, where a softmax
+    row is nearly one-hot (C4), the fp16 rounding of the dominant P entry that multiplies V
+    (relative 2^-11; the running max is raised lazily, so that entry lies in [1, 256) and is
+    rounded, where an eagerly raised max makes it exactly 1). The reference kernel's own error
+    against the same oracle reaches 1.9e-3 on C4.
 The test fails (it does not skip) when the reference build is missing on a GPU machine.
 """
 from __future__ import annotations
@@ -39,7 +43,7 @@ CONFIGS = {
     "C5_b128h16n512_uniform": ((2048, 512, 64), "uniform", 1.0),
 }
 ATOL_REF, RTOL_REF = 2e-3, 1e-2
-ATOL_FP32, RTOL_FP32_ABOVE_2 = 1e-3, 1e-3
+ATOL_FP32, RTOL_FP32 = 1e-3, 1e-3
 SCORE_BYTES_PER_CHUNK = 1 << 30  # fp32 score block of the chunked oracle
 
 
@@ -97,13 +101,14 @@ def test_whole_output_matches_reference_kernel_and_fp32(name):
     exact = naive_fp32_chunked(q, k, v)
     err = (ours.float() - exact).abs()
     big = exact.abs() > 2
-    bound = torch.where(big, ATOL_FP32 + RTOL_FP32_ABOVE_2 * exact.abs(),
-                        torch.full_like(exact, ATOL_FP32))
+    bound = ATOL_FP32 + RTOL_FP32 * exact.abs()
     err_theirs = (theirs.float() - exact).abs()
     # the figures for the record (pytest -s), the reference kernel against the same oracle too
     print(f"\n{name}: max|ours-ref|={diff_ref.max().item():.3e} "
           f"max|ours-fp32|={err.max().item():.3e} (|o|<=2: {err[~big].max().item():.3e}) "
-          f"max|ref-fp32|={err_theirs.max().item():.3e} max|o|={exact.abs().max().item():.3f}")
+          f"max|ref-fp32|={err_theirs.max().item():.3e} (|o|<=2: "
+          f"{err_theirs[~big].max().item():.3e}) max|o|={exact.abs().max().item():.3f} "
+          f"max err/bound={(err / bound).max().item():.3f}")
 
     torch.testing.assert_close(ours, theirs, atol=ATOL_REF, rtol=RTOL_REF)
     worst = int((err - bound).argmax())
