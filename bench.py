@@ -536,7 +536,7 @@ def run_ours(args, wl) -> dict | None:
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     default_mode = not train and d == D and dtype == torch.float16 and not causal
-    traffic = load_traffic("mfa_fwd", args.workload) if default_mode else None
+    traffic = load_traffic("mfa_fwd", args.workload) if default_mode and q_range is None else None
     e2e_value = None if e2e_ms is None else job_flops_step * e2e_steps / (e2e_ms / 1e3) / 1e12
     bytes_in = 3 * global_bh * n * d * 2
     bytes_out = global_bh * n * d * 2
@@ -578,6 +578,11 @@ def run_ours(args, wl) -> dict | None:
             "frac": round(achieved / peak, 4),
             "traffic": traffic,
             "algorithmic_bytes": attention_bytes(bh, n, d),
+            # the memory side of the same call: q, k, v read once and out written once
+            "hbm": {"achieved_gbs": round(attention_bytes(bh, n, d) / (kernel_ms / 1e3) / 1e9, 1),
+                    "peak_gbs": float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
+                    "frac": round(attention_bytes(bh, n, d) / (kernel_ms / 1e3) / 1e9
+                                  / float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])), 4)},
             "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops burst)"
             if peak_src == "measured" else "fallback 1.59 PFLOP/s",
             "kernel": "mfa_fwd_kernel<2,3> (+ mfa_merge_kernel when the key dimension is split); "
