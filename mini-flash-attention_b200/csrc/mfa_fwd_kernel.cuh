@@ -18,7 +18,12 @@
 //                     softmax warps never wait for one another.
 //   warp  8*NQ      : MMA issuer (whole warp, one elected lane issues): S_i = Q_i K^T (SS
 //                     form) and O_i += P_i V (TS form: P straight from TMEM, V consumed
-//                     MN-major, so no transpose).
+//                     MN-major, so no transpose). With two query tiles it issues tile 0's
+//                     products and warp 8*NQ+3 issues tile 1's: one thread issues a
+//                     tcgen05.mma about every 60-70 cycles, more than a 128x64x16 P.V
+//                     product takes on the tensor core (32 cycles), so a single issuer
+//                     cannot keep the tensor core busy (measured: the same MMA stream with
+//                     no softmax in the way runs 1.29x faster from two warps).
 //   warp  8*NQ+1    : TMA producer: the Q tiles of each unit (two Q buffers, so the next
 //                     unit's Q loads while this one runs), then K and V blocks.
 //   warp  8*NQ+2    : (NQ = 2) TMA stores of finished units' output (staged in their Q
@@ -68,14 +73,17 @@ struct FwdConfig {
   static constexpr int kSoftmaxWarps = 8 * NQ;   // two warps per TMEM lane quadrant and tile
   static constexpr int kMmaWarp = kSoftmaxWarps;
   static constexpr int kLoadWarp = kSoftmaxWarps + 1;
-  // Output stores of finished units: a store warp with two query tiles (it fills the fifth
-  // warpgroup, otherwise idle); with one tile the first softmax warp of the tile issues them
+  // Output stores of finished units: a store warp with two query tiles (in the fifth
+  // warpgroup); with one tile the first softmax warp of the tile issues them
   // (a third non-softmax warp next to two softmax warps per sub-partition measured slower).
   static constexpr bool kStoreRole = NQ == 2;
   static constexpr int kStoreWarp = kSoftmaxWarps + 2;
+  // MMA issuers: one per query tile (tile 1's is the fifth warpgroup's fourth warp). Each
+  // commits once per step on the K / V empty barriers, which therefore count NQ arrivals.
+  static constexpr int kMmaWarp2 = kSoftmaxWarps + 3;
   // With two query tiles (16 softmax warps) the register file is rebalanced with setmaxnreg,
-  // which works per warpgroup: the MMA, load and store warps then fill a fifth warpgroup
-  // (1 warp idle). 640 threads launch with 96 registers each (5 warps per SM
+  // which works per warpgroup: the two MMA warps, the load and the store warp then fill a
+  // fifth warpgroup. 640 threads launch with 96 registers each (5 warps per SM
   // sub-partition); after the split: 512 x 104 + 128 x 64 = 640 x 96, and per sub-partition
   // 4 x 104 + 64 <= 512.
   static constexpr bool kRebalanceRegs = NQ == 2;
@@ -101,8 +109,8 @@ struct FwdConfig {
   static constexpr int kBarPFull = kBarSFree + NQ;
   static constexpr int kBarODone = kBarPFull + NQ;
   static constexpr int kBarStage = kBarODone + NQ;  // [tile]: output staging written
-  static constexpr int kBarDrain = kBarStage + NQ;
-  static constexpr int kNumBars = kBarDrain + 1;
+  static constexpr int kBarDrain = kBarStage + NQ;  // [NQ]: one per MMA warp
+  static constexpr int kNumBars = kBarDrain + NQ;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kSmemUsed = kAbortOff + 4;
@@ -293,10 +301,12 @@ __device__ __forceinline__ void load_role(const FwdParams& p, uint8_t* smem, uin
 // datapath, no per-MMA register moves); one elected lane issues tcgen05.mma / commit. Issue
 // cost per MMA matters here: a 128x64x16 P.V step is only 32 tensor-core cycles. S for step
 // g+1 is issued before P.V of step g, so the next scores are computed while the softmax warps
-// still work on the current block (also across unit boundaries).
+// still work on the current block (also across unit boundaries). Each MMA warp issues the
+// products of one query tile, so each tile's products follow its own softmax warps and no tile
+// waits for the other's P.
 template <class Cfg>
 __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint32_t bars,
-                                         uint32_t tmem, const Watchdog& wd) {
+                                         uint32_t tmem, const Watchdog& wd, int tile) {
   constexpr int ST = Cfg::STAGES;
   constexpr int NQ = Cfg::NQ;
   auto bar = [&](int idx) { return bars + 8u * static_cast<uint32_t>(idx); };
@@ -339,8 +349,8 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
     if (!wait_warp(bar(Cfg::kBarKFull + st), static_cast<uint32_t>(gs / ST) & 1u, wd, kSiteMmaK))
       return false;
     const uint32_t kd = k_lo + st * kTileStep;
-#pragma unroll
-    for (int i = 0; i < NQ; ++i) {
+    {
+      const int i = tile;
       if (gs > 0) {
         if (!wait_warp(bar(Cfg::kBarSFree + i), static_cast<uint32_t>(gs - 1) & 1u, wd,
                        kSiteMmaSFree))
@@ -379,8 +389,8 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
         goto unwind;
       const uint32_t vd = v_lo + st * kTileStep;
       const bool fresh = cp.first_step();  // first block of a unit: overwrite O
-#pragma unroll
-      for (int i = 0; i < NQ; ++i) {
+      {
+        const int i = tile;
         if (!wait_warp(bar(Cfg::kBarPFull + i), static_cast<uint32_t>(gp) & 1u, wd,
                        kSiteMmaPFull))
           goto unwind;
@@ -409,9 +419,9 @@ __device__ __forceinline__ void mma_role(const FwdParams& p, uint8_t* smem, uint
 unwind:
   if (issued_any) {
     // Let every MMA this warp issued finish before TMEM is released.
-    if (leader) mma_commit(bar(Cfg::kBarDrain));
+    if (leader) mma_commit(bar(Cfg::kBarDrain + tile));
     __syncwarp();
-    drain_wait(bar(Cfg::kBarDrain), 0);
+    drain_wait(bar(Cfg::kBarDrain + tile), 0);
   }
 }
 
@@ -765,9 +775,9 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
       }
       for (int s = 0; s < STAGES; ++s) {
         mbar_init(bars + 8 * (Cfg::kBarKFull + s), 1);
-        mbar_init(bars + 8 * (Cfg::kBarKEmpty + s), 1);
+        mbar_init(bars + 8 * (Cfg::kBarKEmpty + s), Cfg::NQ);
         mbar_init(bars + 8 * (Cfg::kBarVFull + s), 1);
-        mbar_init(bars + 8 * (Cfg::kBarVEmpty + s), 1);
+        mbar_init(bars + 8 * (Cfg::kBarVEmpty + s), Cfg::NQ);
       }
       for (int i = 0; i < NQ; ++i) {
         mbar_init(bars + 8 * (Cfg::kBarSFull + i), 1);
@@ -776,7 +786,7 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
         mbar_init(bars + 8 * (Cfg::kBarODone + i), 1);
       }
       for (int i = 0; i < NQ; ++i) mbar_init(bars + 8 * (Cfg::kBarStage + i), 8);
-      mbar_init(bars + 8 * Cfg::kBarDrain, 1);
+      for (int i = 0; i < NQ; ++i) mbar_init(bars + 8 * (Cfg::kBarDrain + i), 1);
       mbar_init_fence();
     }
     __syncwarp();
@@ -801,8 +811,8 @@ __global__ void __launch_bounds__(FwdConfig<NQ, STAGES, CAUSAL, BF16, D, LSE>::k
       softmax_role<Cfg>(p, smem, bars, tmem, warp / 8, wd);
     } else {
       if constexpr (Cfg::kRebalanceRegs) setmaxnreg_dec<Cfg::kControlRegs>();
-      if (warp == Cfg::kMmaWarp) {
-        mma_role<Cfg>(p, smem, bars, tmem, wd);
+      if (warp == Cfg::kMmaWarp || (Cfg::NQ == 2 && warp == Cfg::kMmaWarp2)) {
+        mma_role<Cfg>(p, smem, bars, tmem, wd, warp == Cfg::kMmaWarp ? 0 : 1);
       } else if (Cfg::kStoreRole && warp == Cfg::kStoreWarp) {
         if (lane == 0) store_role<Cfg>(p, smem, bars, wd);
       }
