@@ -67,11 +67,15 @@ struct BwdConfig {
   static constexpr int kTileBytes = kRows * kHeadDim * 2;
   static constexpr int STAGES = 3;
   static constexpr int kSoftmaxWarps = 16;  // 16 rows x 64 columns each
+  // Two MMA issuers: warp 16 the S and dP products (SS), warp 19 the accumulations (TS). One
+  // thread issues a tcgen05.mma only every few tens of cycles, and a step has 24 products in
+  // the dK/dV pass (16 in the dQ pass), most of them 128x64x16 (32 tensor-core cycles each).
   static constexpr int kMmaWarp = 16;
   static constexpr int kLoadWarp = 17;
   static constexpr int kStoreWarp = 18;  // TMA stores of finished units' gradients
-  // As in the forward kernel: 640 threads (the MMA, load and store warps fill a fifth
-  // warpgroup, 1 warp idle) launch with 96 registers; setmaxnreg moves the control warpgroup to 64 and
+  static constexpr int kAccWarp = 19;
+  // As in the forward kernel: 640 threads (the two MMA warps, the load and the store warp fill
+  // a fifth warpgroup) launch with 96 registers; setmaxnreg moves the control warpgroup to 64 and
   // the four softmax-side warpgroups to 104 (512 x 104 + 128 x 64 = 640 x 96; per SM
   // sub-partition 4 x 104 + 64 <= 512 registers per lane).
   static constexpr int kThreads = 32 * 20;
@@ -93,8 +97,8 @@ struct BwdConfig {
   static constexpr int kBarOpFull = kBarSSFree + 1;         // fp16 operands written (16 warps)
   static constexpr int kBarAccDone = kBarOpFull + 1;        // TS MMAs of a step completed
   static constexpr int kBarStage = kBarAccDone + 1;         // output staging written (16 warps)
-  static constexpr int kBarDrain = kBarStage + 1;
-  static constexpr int kNumBars = kBarDrain + 1;
+  static constexpr int kBarDrain = kBarStage + 1;  // [2]: one per MMA issuer
+  static constexpr int kNumBars = kBarDrain + 2;
   static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
   static constexpr int kAbortOff = kTmemSlotOff + 4;
   static constexpr int kSmemBytes = kAbortOff + 4 + 1024;
@@ -246,7 +250,10 @@ __device__ __forceinline__ void bwd_load_role(const BwdParams& p, uint8_t* smem,
   }
 }
 
-template <class Cfg>
+// kAcc false: the S and dP products of every step (warp kMmaWarp); kAcc true: the
+// accumulations into dQ, or dV and dK (warp kAccWarp). Both read the streamed stage, whose
+// empty barrier counts one commit from each.
+template <class Cfg, bool kAcc>
 __device__ __forceinline__ void bwd_mma_role(const BwdParams& p, uint8_t* smem, uint32_t bars,
                                              uint32_t tmem, const Watchdog& wd) {
   constexpr int ST = Cfg::STAGES;
@@ -294,6 +301,7 @@ __device__ __forceinline__ void bwd_mma_role(const BwdParams& p, uint8_t* smem, 
         mma_ss(tmem + Cfg::kColDP, desc_join(yd + 2 * kk, kHi), desc_join(s1 + 2 * kk, kHi),
                kIdescSS, kk > 0 ? 1u : 0u);
       mma_commit(bar(Cfg::kBarSSFull));
+      mma_commit(bar(Cfg::kBarStrEmpty + st));
     }
     __syncwarp();
     issued_any = true;
@@ -302,11 +310,17 @@ __device__ __forceinline__ void bwd_mma_role(const BwdParams& p, uint8_t* smem, 
     return true;
   };
 
-  if (cs.valid() && !issue_ss()) goto unwind;
-  while (cp.valid()) {
-    if (cs.valid() && !issue_ss()) goto unwind;
+  if (!kAcc) {
+    while (cs.valid())
+      if (!issue_ss()) goto unwind;
+  }
+  while (kAcc && cp.valid()) {
     {
       const int st = gp % ST;
+      // the stage's tiles are this thread's operands too
+      if (!wait_warp(bar(Cfg::kBarStrFull + st), static_cast<uint32_t>(gp / ST) & 1u, wd,
+                     kSiteMmaK))
+        goto unwind;
       if (!wait_warp(bar(Cfg::kBarOpFull), static_cast<uint32_t>(gp) & 1u, wd, kSiteMmaPFull))
         goto unwind;
       tc_fence_after();
@@ -332,6 +346,7 @@ __device__ __forceinline__ void bwd_mma_role(const BwdParams& p, uint8_t* smem, 
         mma_commit(bar(Cfg::kBarStrEmpty + st));
       }
       __syncwarp();
+      issued_any = true;
       ++gp;
       cp.step(p);
     }
@@ -339,17 +354,18 @@ __device__ __forceinline__ void bwd_mma_role(const BwdParams& p, uint8_t* smem, 
   // Every commit of this pass has arrived before the role returns (the barriers may be
   // initialised again for a second pass).
   if (issued_any) {
-    if (leader) mma_commit(bar(Cfg::kBarDrain));
+    if (leader) mma_commit(bar(Cfg::kBarDrain + (kAcc ? 1 : 0)));
     __syncwarp();
-    wait_warp(bar(Cfg::kBarDrain), 0, wd, kSiteMmaDrain);  // on failure the CTA unwinds
+    // on failure the CTA unwinds
+    wait_warp(bar(Cfg::kBarDrain + (kAcc ? 1 : 0)), 0, wd, kSiteMmaDrain);
   }
   return;
 
 unwind:
   if (issued_any) {
-    if (leader) mma_commit(bar(Cfg::kBarDrain));
+    if (leader) mma_commit(bar(Cfg::kBarDrain + (kAcc ? 1 : 0)));
     __syncwarp();
-    drain_wait(bar(Cfg::kBarDrain), 0);
+    drain_wait(bar(Cfg::kBarDrain + (kAcc ? 1 : 0)), 0);
   }
 }
 
@@ -580,7 +596,7 @@ __device__ __forceinline__ void bwd_init_bars(uint32_t bars) {
   }
   for (int s = 0; s < Cfg::STAGES; ++s) {
     mbar_init(bars + 8 * (Cfg::kBarStrFull + s), 1);
-    mbar_init(bars + 8 * (Cfg::kBarStrEmpty + s), 1);
+    mbar_init(bars + 8 * (Cfg::kBarStrEmpty + s), 2);  // both MMA issuers read the stage
   }
   mbar_init(bars + 8 * Cfg::kBarSSFull, 1);
   mbar_init(bars + 8 * Cfg::kBarSSFree, Cfg::kSoftmaxWarps);
@@ -588,6 +604,7 @@ __device__ __forceinline__ void bwd_init_bars(uint32_t bars) {
   mbar_init(bars + 8 * Cfg::kBarAccDone, 1);
   mbar_init(bars + 8 * Cfg::kBarStage, Cfg::kSoftmaxWarps);
   mbar_init(bars + 8 * Cfg::kBarDrain, 1);
+  mbar_init(bars + 8 * (Cfg::kBarDrain + 1), 1);
   mbar_init_fence();
 }
 
@@ -667,14 +684,18 @@ __device__ __forceinline__ void bwd_cta(const BwdParams& pa, const BwdParams& pb
     } else {
       setmaxnreg_dec<CA::kControlRegs>();
       if (warp == CA::kMmaWarp) {
-        bwd_mma_role<CA>(pa, smem, bars, tmem, wd);
+        bwd_mma_role<CA, false>(pa, smem, bars, tmem, wd);
+      } else if (warp == CA::kAccWarp) {
+        bwd_mma_role<CA, true>(pa, smem, bars, tmem, wd);
       } else if (warp == CA::kStoreWarp) {
         if (lane == 0) bwd_store_role<CA>(pa, smem, bars, wd);
       }
       if constexpr (kTwo) {
         if (next_pass()) {
           if (warp == CB::kMmaWarp) {
-            bwd_mma_role<CB>(pb, smem, bars, tmem, wd);
+            bwd_mma_role<CB, false>(pb, smem, bars, tmem, wd);
+          } else if (warp == CB::kAccWarp) {
+            bwd_mma_role<CB, true>(pb, smem, bars, tmem, wd);
           } else if (warp == CB::kStoreWarp) {
             if (lane == 0) bwd_store_role<CB>(pb, smem, bars, wd);
           }
