@@ -25,7 +25,10 @@ carries, for the default forward:
   kernel_only     CUDA events around the C-ABI call mfa_fwd_f16 (no torch allocation or
                   binding), same buffers, flush and steps: the kernels alone;
   kernel_us       per-kernel device durations of three flushed calls from a CUPTI trace;
-  strong          the strong splits of B16 H16 N4096 (256 batch*head rows contiguous over the
+  memory          device memory a call takes beyond its inputs: the torch allocator's peak
+                  (the reference benchmark's figure: the output) and the split plan's scratch
+                  from the library's own pool;
+  strong         the strong splits of B16 H16 N4096 (256 batch*head rows contiguous over the
                   ranks) and B1 H32 N32768 (its 32 heads over the ranks), timed in the same
                   process after the headline, max over ranks;
   reference_kernel (one GPU) a GPU baseline leg: the reference's own CuTe kernel (compiled from
@@ -307,6 +310,34 @@ def time_calls(fn, inputs, flush, stream, steps: int, warmup: int) -> list[float
 STRONG = (("b16h16n4096", 3, 10), ("b1h32n32768", 3, 5))
 
 
+def extra_memory(fwd, inputs, flush, bh: int, n: int, d: int, causal: bool) -> dict:
+    """Device memory a forward call takes beyond its inputs, as the reference's benchmark counts
+    it (benchs/benchmark_forward.py:262-289: the torch allocator's peak over the calls above the
+    memory held before them, i.e. the output tensor), and the split plan's partial-result
+    scratch, which the library takes from its own stream-ordered pool, outside torch's count
+    (mfa_fwd_workspace_bytes)."""
+    from mini_flash_attention import capi
+
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    for i in range(3):
+        flush.fill_(1.0)
+        out = fwd(*inputs[i % len(inputs)])
+        del out
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated() - base
+    ws = capi.fwd_workspace_bytes(1, bh, n, d, causal)
+    q = inputs[0][0]
+    return {"allocator_peak_bytes": int(peak),
+            "output_bytes": q.numel() * q.element_size(),
+            "workspace_bytes": int(ws),
+            "total_extra_bytes": int(peak + ws),
+            "method": "torch.cuda.max_memory_allocated() - memory_allocated() over 3 flushed "
+                      "calls (the reference benchmark's figure) + the workspace from the "
+                      "library's pool (mfa_fwd_workspace_bytes)"}
+
+
 def strong_splits(rank: int, world: int, dev, flush, stream) -> dict:
     """B16 H16 N4096 and B1 H32 N32768 with their global batch*head rows split contiguously
     over the ranks (no collective on the data path); whole-job TFLOPS from the max over ranks."""
@@ -509,6 +540,7 @@ def run_ours(args, wl) -> dict | None:
                 "timing": "CUDA events around the C-ABI call mfa_fwd_f16, same buffers, flush "
                           "and step count as value, max over ranks"}
             extras["kernel_us"] = kernel_durations(fwd, inputs, flush)
+            extras["memory"] = extra_memory(fwd, inputs, flush, bh, n, d, causal)
             if not causal:
                 extras["strong"] = strong_splits(rank, world, dev, flush, stream)
             if world == 1:

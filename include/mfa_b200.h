@@ -121,6 +121,20 @@ MFA_API int mfa_bwd(const void* q, const void* k, const void* v, const void* out
                     int64_t batch, int64_t heads, int64_t n, int32_t d, float scale,
                     int32_t causal, int32_t dtype, int32_t layout, void* stream);
 
+/*
+ * Device scratch, in bytes, that one call of mfa_fwd (or mfa_fwd_f16 / mfa_fwd_lse, and with d
+ * = 64 and fp16 mfa_fwd_f16_noalloc) takes on the current device for these extents: 0 when
+ * whole query blocks fill the SMs evenly, else the split plan's partial-result slots (2 x
+ * (256 rows x (D + 2) floats) per CTA, one CTA per SM). dtype and layout do not change it.
+ * Nothing is launched or allocated. The allocating entry points take it from a stream-ordered
+ * pool of the library (outside any framework allocator) and return it on the same stream;
+ * the output tensor is the caller's. No counterpart in the reference, whose launchers need
+ * no scratch (its benchmark reports the allocator's peak over the calls,
+ * benchs/benchmark_forward.py:266-289).
+ */
+MFA_API int mfa_fwd_workspace_bytes(int64_t batch, int64_t heads, int64_t n, int32_t d,
+                                    int32_t causal, uint64_t* bytes);
+
 /* Size of the static device scratch array used by mfa_fwd_f16_noalloc (20 MiB). */
 #define MFA_NOALLOC_SCRATCH_BYTES 20971520u
 

@@ -902,6 +902,47 @@ extern "C" int mfa_fwd_f16_noalloc(const void* q, const void* k, const void* v, 
                 : launch_forward_noalloc<Full<false, false>>(q, k, v, out, bh, n, scale, s);
 }
 
+namespace mfa {
+namespace {
+template <class Cfg>
+int workspace_of(int64_t bh, int64_t n, int64_t sms, uint64_t* bytes) {
+  Plan pl;
+  const int rc = plan_forward<Cfg>(bh, n, n, sms, pl);
+  if (rc == MFA_OK) *bytes = pl.workspace_bytes;
+  return rc;
+}
+}  // namespace
+}  // namespace mfa
+
+// The plan only: nothing is launched or allocated, and the answer is the size that
+// launch_forward takes from its pool (or, for D = 64 fp16, mfa_fwd_f16_noalloc from its array).
+extern "C" int mfa_fwd_workspace_bytes(int64_t batch, int64_t heads, int64_t n, int32_t d,
+                                       int32_t causal, uint64_t* bytes) {
+  if (!bytes) return fail(MFA_ERR_INVALID_ARGUMENT, "bytes must not be null");
+  *bytes = 0;
+  if (batch < 0 || heads < 0 || n < 0) return fail(MFA_ERR_INVALID_ARGUMENT, "negative extent");
+  if (heads > 0 && batch > 0x7fffffffLL / heads)
+    return fail(MFA_ERR_INVALID_ARGUMENT, "B * H is too large");
+  if (n > 0x7fffffffLL) return fail(MFA_ERR_INVALID_ARGUMENT, "N is too large");
+  if (d != 32 && d != 64 && d != 128)
+    return fail(MFA_ERR_HEAD_DIM, "This kernel supports only D=32, D=64 and D=128");
+  const int64_t bh = batch * heads;
+  if (bh == 0 || n == 0) return MFA_OK;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaDeviceGetAttribute (multiprocessor count)");
+  // dtype, layout and the log-sum-exp option do not change the plan
+  if (d == 32)
+    return causal ? workspace_of<Full<true, false, 32>>(bh, n, sms, bytes)
+                  : workspace_of<Full<false, false, 32>>(bh, n, sms, bytes);
+  if (d == 128)
+    return causal ? workspace_of<Full<true, false, 128>>(bh, n, sms, bytes)
+                  : workspace_of<Full<false, false, 128>>(bh, n, sms, bytes);
+  return causal ? workspace_of<Full<true, false>>(bh, n, sms, bytes)
+                : workspace_of<Full<false, false>>(bh, n, sms, bytes);
+}
+
 extern "C" const char* mfa_last_error_string(void) { return g_last_error.c_str(); }
 
 extern "C" int mfa_device_status(int device, int* status, int reset) {

@@ -19,6 +19,7 @@ EXPORTED_SYMBOLS = (
     "mfa_fwd_rows",
     "mfa_fwd_lse",
     "mfa_bwd",
+    "mfa_fwd_workspace_bytes",
     "mfa_last_error_string",
     "mfa_device_status",
     "mfa_set_watchdog_ns",
@@ -91,6 +92,10 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
     lib.mfa_watchdog_selftest.restype = ctypes.c_int
     lib.mfa_version.argtypes = []
     lib.mfa_version.restype = ctypes.c_char_p
+    lib.mfa_fwd_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.POINTER(ctypes.c_uint64)]
+    lib.mfa_fwd_workspace_bytes.restype = ctypes.c_int
     if path is None:
         _LIB = lib
     return lib
@@ -144,6 +149,15 @@ def bwd(q_ptr: int, k_ptr: int, v_ptr: int, o_ptr: int, do_ptr: int, lse_ptr: in
     """Launch mfa_bwd; raises MfaError."""
     _check(load().mfa_bwd(q_ptr, k_ptr, v_ptr, o_ptr, do_ptr, lse_ptr, dq_ptr, dk_ptr, dv_ptr,
                           batch, heads, n, d, scale, int(causal), dtype, layout, stream))
+
+
+def fwd_workspace_bytes(batch: int, heads: int, n: int, d: int = 64,
+                        causal: bool = False) -> int:
+    """Device scratch bytes one forward call takes on the current device (0 unless the
+    key dimension is split); nothing is launched or allocated. Raises MfaError."""
+    out = ctypes.c_uint64(0)
+    _check(load().mfa_fwd_workspace_bytes(batch, heads, n, d, int(causal), ctypes.byref(out)))
+    return out.value
 
 
 def device_status(device: int = 0, reset: bool = True) -> int:

@@ -163,3 +163,13 @@ def test_general_entry_validates_dtype_layout_and_shape():
     assert call().code in (capi.MFA_ERR_CUDA, capi.MFA_ERR_DEVICE)
     # empty problems are no-ops
     capi.fwd_general(FAKE, FAKE, FAKE, FAKE, 0, 3, 256, 64, 0.125)
+
+
+def test_workspace_query_rejects_bad_arguments():
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd_workspace_bytes(1, 8, 1024, d=48)
+    assert e.value.code == capi.MFA_ERR_HEAD_DIM
+    with pytest.raises(capi.MfaError) as e:
+        capi.fwd_workspace_bytes(-1, 8, 1024)
+    assert e.value.code == capi.MFA_ERR_INVALID_ARGUMENT
+    assert capi.fwd_workspace_bytes(0, 8, 1024) == 0  # empty: no device needed

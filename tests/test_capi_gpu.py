@@ -70,3 +70,20 @@ def test_device_status_clean_after_many_launches():
         capi.fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), 16, 2048, 64, 0.125,
                  stream=s)
     assert capi.device_status(torch.cuda.current_device()) == 0
+
+
+def test_workspace_query_matches_the_plan():
+    """mfa_fwd_workspace_bytes: zero when whole 256-row query blocks fill the SMs evenly, else
+    two partial-result slots of 256 rows x (D + 2) floats per SM."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    slot = lambda d: 256 * (d + 2) * 4  # noqa: E731
+    # 256 query blocks on 148 SMs: split
+    assert capi.fwd_workspace_bytes(1, 8, 8192) == 2 * sms * slot(64)
+    assert capi.fwd_workspace_bytes(1, 8, 8192, d=32) == 2 * sms * slot(32)
+    # 4096 query blocks (27.7 waves): whole blocks
+    assert capi.fwd_workspace_bytes(16, 16, 4096) == 0
+    # causal masking always splits; fewer steps than SMs use fewer CTAs
+    assert capi.fwd_workspace_bytes(16, 16, 4096, causal=True) == 2 * sms * slot(64)
+    assert 0 < capi.fwd_workspace_bytes(1, 1, 256, causal=True) < 2 * sms * slot(64)
+    # the no-alloc entry point's array covers every D = 64 plan on this device
+    assert capi.fwd_workspace_bytes(1, 8, 8192) <= capi.NOALLOC_SCRATCH_BYTES
