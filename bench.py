@@ -28,12 +28,14 @@ carries, for the default forward:
   memory          device memory a call takes beyond its inputs: the torch allocator's peak
                   (the reference benchmark's figure: the output) and the split plan's scratch
                   from the library's own pool;
-  strong         the strong splits of B16 H16 N4096 (256 batch*head rows contiguous over the
+  strong          the strong splits of B16 H16 N4096 (256 batch*head rows contiguous over the
                   ranks) and B1 H32 N32768 (its 32 heads over the ranks), timed in the same
                   process after the headline, max over ranks;
   reference_kernel (one GPU) a GPU baseline leg: the reference's own CuTe kernel (compiled from
                   its sources into oracle/_ref) on the same buffers, flush and events, timed
                   after everything else, like cpu_baseline;
+  cudnn_sdpa      (one GPU) context: cuDNN's fused attention (torch SDPA, cuDNN backend) on
+                  the same buffers, flush and events;
   e2e.copy_gbs    host<->device bytes of one rank's step / that rank's e2e time per step.
 --no-extras leaves all of these out (for profiler runs).
 
@@ -385,6 +387,30 @@ def reference_kernel_leg(wl: dict, inputs, flush, stream, steps: int, warmup: in
                       "zeros_like output inside the timed call (flash_attn.cpp:86)"}
 
 
+def cudnn_leg(inputs, flush, stream, steps: int, warmup: int, causal: bool) -> dict:
+    """Context leg: NVIDIA's fused attention from cuDNN (torch scaled_dot_product_attention with
+    the cuDNN backend) on the same buffers, viewed [1, B*H, N, D], same flush and events. A
+    library kernel, not on this library's path: it shows where the forward stands against the
+    vendor's own B200 kernel on the same box."""
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        def run(q, k, v):
+            return torch.nn.functional.scaled_dot_product_attention(
+                q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), is_causal=causal)
+
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            ms = time_calls(run, inputs, flush, stream, steps, warmup)
+    except Exception as exc:  # noqa: BLE001  (a context leg must not break the bench line)
+        return {"value": None, "reason": f"{type(exc).__name__}: {str(exc)[:160]}"}
+    bh, n, d = inputs[0][0].shape
+    t = sum(ms) / steps
+    return {"value": round(attention_flops(bh, n, d, causal) / (t / 1e3) / 1e12, 3),
+            "unit": UNIT, "ms_per_step": round(t, 4), "steps": steps, "warmup": warmup,
+            "kernel": "cuDNN fused attention via torch SDPA (SDPBackend.CUDNN_ATTENTION), "
+                      f"cuDNN {torch.backends.cudnn.version()}"}
+
+
 # ---------------------------------------------------------------- arms
 def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -546,6 +572,7 @@ def run_ours(args, wl) -> dict | None:
             if world == 1:
                 extras["reference_kernel"] = reference_kernel_leg(
                     wl, inputs, flush, stream, max(3, min(args.steps, 20)), 3)
+                extras["cudnn_sdpa"] = cudnn_leg(inputs, flush, stream, args.steps, 3, causal)
 
     if world > 1:
         import torch.distributed as dist
