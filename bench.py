@@ -29,11 +29,13 @@ carries, for the default forward:
                   (the reference benchmark's figure: the output) and the split plan's scratch
                   from the library's own pool;
   strong          the strong splits of B16 H16 N4096 (256 batch*head rows contiguous over the
-                  ranks) and B1 H32 N32768 (its 32 heads over the ranks), timed in the same
+                  ranks), B1 H32 N32768 (its 32 heads over the ranks) and B128 H16 N512 (2048
+                  rows over the ranks), timed in the same
                   process after the headline, max over ranks;
   reference_kernel (one GPU) a GPU baseline leg: the reference's own CuTe kernel (compiled from
                   its sources into oracle/_ref) on the same buffers, flush and events, timed
                   after everything else, like cpu_baseline;
+  modes           (one GPU, headline) causal, bf16, D=128 and the backward pass at B1 H8 N8192;
   cudnn_sdpa      (one GPU) context: cuDNN's fused attention (torch SDPA, cuDNN backend) on
                   the same buffers, flush and events;
   e2e.copy_gbs    host<->device bytes of one rank's step / that rank's e2e time per step.
@@ -309,7 +311,7 @@ def time_calls(fn, inputs, flush, stream, steps: int, warmup: int) -> list[float
 
 
 # strong splits measured after the headline: (workload, warm-up calls, timed calls)
-STRONG = (("b16h16n4096", 3, 10), ("b1h32n32768", 3, 5))
+STRONG = (("b16h16n4096", 3, 10), ("b1h32n32768", 3, 5), ("b128h16n512", 3, 10))
 
 
 def extra_memory(fwd, inputs, flush, bh: int, n: int, d: int, causal: bool) -> dict:
@@ -341,8 +343,9 @@ def extra_memory(fwd, inputs, flush, bh: int, n: int, d: int, causal: bool) -> d
 
 
 def strong_splits(rank: int, world: int, dev, flush, stream) -> dict:
-    """B16 H16 N4096 and B1 H32 N32768 with their global batch*head rows split contiguously
-    over the ranks (no collective on the data path); whole-job TFLOPS from the max over ranks."""
+    """B16 H16 N4096, B1 H32 N32768 and B128 H16 N512 with their global batch*head rows split
+    contiguously over the ranks (no collective on the data path); whole-job TFLOPS from the max
+    over ranks."""
     import mini_flash_attention as mfa
     from mini_flash_attention.sharding import bh_shard
 
@@ -363,6 +366,38 @@ def strong_splits(rank: int, world: int, dev, flush, stream) -> dict:
                      "warmup": warmup,
                      "split": f"{global_bh} batch*head rows contiguous over {world} GPU(s)"}
         del inputs
+    return out
+
+
+def mode_legs(dev, flush, stream, steps: int = 20, warmup: int = 3) -> dict:
+    """The headline shape (B1 H8 N8192) in the library's other modes, same flush and events:
+    causal fp16 (flops over the N(N+1)/2 attended pairs), bf16, D = 128, and the backward pass
+    (mfa.backward from forward_lse's output; flops 2.5x the forward's, the usual convention)."""
+    import mini_flash_attention as mfa
+
+    wl = WORKLOADS["b1h8n8192"]
+    bh, n = wl["B"] * wl["H"], wl["N"]
+    out = {}
+    for name, d, dtype, causal in (("causal", D, torch.float16, True),
+                                   ("bf16", D, torch.bfloat16, False),
+                                   ("d128", 128, torch.float16, False)):
+        inputs = [make_inputs(wl, bh, 200 + i, dev, d=d, dtype=dtype) for i in range(2)]
+        ms = time_calls(lambda q, k, v, c=causal: mfa.forward(q, k, v, causal=c), inputs, flush,
+                        stream, steps, warmup)
+        t = sum(ms) / steps
+        out[name] = {"ms_per_step": round(t, 4), "unit": UNIT,
+                     "value": round(attention_flops(bh, n, d, causal) / (t / 1e3) / 1e12, 3)}
+        del inputs
+    prepared = []
+    for i in range(2):
+        q, k, v, do = make_inputs(wl, bh, 210 + i, dev, with_grad=True)
+        o, lse = mfa.forward_lse(q, k, v)
+        prepared.append((q, k, v, o, lse, do))
+    ms = time_calls(lambda q, k, v, o, lse, do: mfa.backward(q, k, v, o, lse, do), prepared,
+                    flush, stream, steps, warmup)
+    t = sum(ms) / steps
+    out["backward"] = {"ms_per_step": round(t, 4), "unit": UNIT,
+                       "value": round(2.5 * attention_flops(bh, n) / (t / 1e3) / 1e12, 3)}
     return out
 
 
@@ -573,6 +608,8 @@ def run_ours(args, wl) -> dict | None:
                 extras["reference_kernel"] = reference_kernel_leg(
                     wl, inputs, flush, stream, max(3, min(args.steps, 20)), 3)
                 extras["cudnn_sdpa"] = cudnn_leg(inputs, flush, stream, args.steps, 3, causal)
+                if not causal and args.workload == "b1h8n8192":
+                    extras["modes"] = mode_legs(dev, flush, stream)
 
     if world > 1:
         import torch.distributed as dist
