@@ -362,6 +362,9 @@ def strong_splits(rank: int, world: int, dev, flush, stream) -> dict:
         job = attention_flops(global_bh, wl["N"])
         out[name] = {"ms_per_step": round(step_ms, 4),
                      "value": round(job / (step_ms / 1e3) / 1e12, 3), "unit": UNIT,
+                     # q, k, v read once and out written once, whole job
+                     "hbm_gbs": round(attention_bytes(global_bh, wl["N"]) / (step_ms / 1e3) / 1e9,
+                                      1),
                      "bh_per_gpu": sh.rows, "global_bh": global_bh, "steps": steps,
                      "warmup": warmup,
                      "split": f"{global_bh} batch*head rows contiguous over {world} GPU(s)"}
