@@ -3,7 +3,9 @@ heads, any N from 1 to 8192 (log-uniform, so short and ragged lengths are common
 64 / 128, fp16 / bf16, causal or not, [B, H, N, D] or [B, N, H, D]. Each case is checked
 against fp32 attention (the reference test's naive oracle, tests/test_forward.py:28-34 of the
 reference, with the causal mask and the log-sum-exp added), so that no combination of the
-plan's modes (whole / split key ranges, merge, tails, masks) escapes the fixed-shape tests."""
+plan's modes (whole / split key ranges, merge, tails, masks) escapes the fixed-shape tests.
+Each forward case also runs a random query row range through forward_rows and, where its
+contract allows (fp16, D = 64, N % 64 == 0), the single-tile kernel behind forward_wmma."""
 from __future__ import annotations
 
 import math
@@ -39,10 +41,18 @@ def randn(shape, seed, dtype):
 
 def fwd_case(i):
     r = random.Random(1000 + i)
-    return dict(i=i, B=r.randint(1, 3), H=r.randint(1, 5),
-                N=int(math.exp(r.uniform(0, math.log(8192)))), D=r.choice([32, 64, 128]),
-                dtype=r.choice([torch.float16, torch.bfloat16]), causal=r.random() < 0.5,
-                bnhd=r.random() < 0.3, seed=7000 + 10 * i)
+    c = dict(i=i, B=r.randint(1, 3), H=r.randint(1, 5),
+             N=int(math.exp(r.uniform(0, math.log(8192)))), D=r.choice([32, 64, 128]),
+             dtype=r.choice([torch.float16, torch.bfloat16]), causal=r.random() < 0.5,
+             bnhd=r.random() < 0.3, seed=7000 + 10 * i)
+    # a query row range of every head for forward_rows (whole 256-row units with the mask)
+    n = c["N"]
+    if c["causal"]:
+        a = 256 * r.randint(0, (n - 1) // 256)
+    else:
+        a = r.randint(0, n - 1)
+    c["rows"] = (a, r.randint(a + 1, n))
+    return c
 
 
 def case_id(c):
@@ -74,6 +84,17 @@ def test_forward_random(c):
     torch.testing.assert_close(out.float(), ref, rtol=tol, atol=tol)
     if lse is not None:
         torch.testing.assert_close(lse, ref_lse, rtol=1e-4, atol=1e-4)
+    if not c["bnhd"]:
+        # the row range alone: its rows as in the whole forward, nothing else written
+        a, b = c["rows"]
+        ro = torch.full_like(q, 3.0)
+        mfa.forward_rows(q, k, v, a, b, out=ro, causal=causal)
+        torch.testing.assert_close(ro[:, :, a:b].float(), ref[:, :, a:b], rtol=tol, atol=tol)
+        assert (ro[:, :, :a] == 3.0).all() and (ro[:, :, b:] == 3.0).all()
+    if D == 64 and dtype == torch.float16 and N % 64 == 0:
+        # the single-tile kernel behind forward_wmma (the reference's N % 64 contract)
+        torch.testing.assert_close(mfa.forward_wmma(q, k, v, causal=causal).float(), ref,
+                                   rtol=tol, atol=tol)
 
 
 def bwd_case(i):
