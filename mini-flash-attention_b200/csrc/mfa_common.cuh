@@ -38,7 +38,11 @@ struct FwdParams {
   float* lse;
 };
 
-// Status codes written to FwdParams::status by the watchdog: kStatusTimeoutBase + site.
+// Status codes written to FwdParams::status by the watchdog: kStatusTimeoutBase + site. The
+// backward kernel reports its corresponding waits under the same codes: resident tiles as
+// kSiteMmaQ, streamed tiles as kSiteMmaK, S / dP read as kSiteMmaSFree / kSiteSoftSFull,
+// the P / dS operands as kSiteMmaPFull, the accumulations as kSiteSoftODone / kSiteSoftOFinal,
+// the streamed L / D slices and the staging as kSiteSoftStage. (11, 12 and 14 are unused.)
 constexpr int kStatusTimeoutBase = 0x100;
 enum WaitSite : int {
   kSiteLoadKEmpty = 1,
@@ -51,10 +55,7 @@ enum WaitSite : int {
   kSiteSoftSFull = 8,
   kSiteSoftODone = 9,
   kSiteSoftOFinal = 10,
-  kSiteSoftExpTok = 11,
-  kSiteMmaStall = 12,
   kSiteLoadQEmpty = 13,
-  kSiteSoftXch = 14,
   kSiteSoftStage = 15,
   kSiteMmaDrain = 16,
 };
