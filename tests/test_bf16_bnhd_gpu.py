@@ -1,6 +1,6 @@
-"""GPU tests of the bf16 inputs and the [B, N, H, D] layout (the second "next" row of the
-survey: the reference benchmark offers --dtype bf16 and converts inputs to [B, N, H, D] for
-flash-attn, benchs/benchmark_forward.py:162-167, 188, 210-215).
+"""GPU tests of the bf16 inputs and the [B, N, H, D] layout (the reference benchmark offers
+--dtype bf16 and converts inputs to [B, N, H, D] for flash-attn,
+benchs/benchmark_forward.py:162-167, 188, 210-215).
 
 bf16 is checked against the fp32 naive oracle with the reference test's tolerance
 (rtol = atol = 1e-2, tests/test_forward.py:38) and a mean-error bound; the layout is checked
