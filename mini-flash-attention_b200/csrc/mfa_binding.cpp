@@ -209,22 +209,31 @@ void flash_attn_forward_rows(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
   if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
 }
 
-// CUDA events of one pipelined call, destroyed on every exit path.
-struct EventSet {
+// CUDA events of the pipelined calls, kept per calling thread and device from one call to the
+// next: creating them costs several microseconds each, on the path before the first copy.
+// Every call drains its streams before it returns, so the next call on the same thread may
+// record them again; other threads have their own.
+struct PipelineEvents {
   std::vector<cudaEvent_t> ev;
-  explicit EventSet(size_t count) : ev(count, nullptr) {
-    for (auto& e : ev) {
-      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
-        e = nullptr;
-        throw std::runtime_error("cudaEventCreateWithFlags failed");
-      }
-    }
-  }
-  ~EventSet() {
+  ~PipelineEvents() {
     for (auto e : ev)
       if (e) cudaEventDestroy(e);
   }
 };
+
+// At least `count` events of `device` (current) for this thread.
+const std::vector<cudaEvent_t>& pipeline_events(int64_t device, size_t count) {
+  thread_local std::vector<PipelineEvents> per_device;
+  if (per_device.size() <= static_cast<size_t>(device)) per_device.resize(device + 1);
+  auto& ev = per_device[device].ev;
+  while (ev.size() < count) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+      throw std::runtime_error("cudaEventCreateWithFlags failed");
+    ev.push_back(e);
+  }
+  return ev;
+}
 
 void check_cuda(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
@@ -262,10 +271,10 @@ void flash_attn_forward_pinned(torch::Tensor q, torch::Tensor k, torch::Tensor v
   const cudaStream_t s_in = at::cuda::getStreamFromPool().stream();
   const cudaStream_t s_run = at::cuda::getStreamFromPool().stream();
   const cudaStream_t s_out = at::cuda::getStreamFromPool().stream();
-  EventSet events(2 * pieces + 1);
+  const std::vector<cudaEvent_t>& ev = pipeline_events(device, 2 * pieces + 1);
   // the device buffers come from the caching allocator on the current stream
-  check_cuda(cudaEventRecord(events.ev[2 * pieces], cur), "cudaEventRecord");
-  check_cuda(cudaStreamWaitEvent(s_in, events.ev[2 * pieces], 0), "cudaStreamWaitEvent");
+  check_cuda(cudaEventRecord(ev[2 * pieces], cur), "cudaEventRecord");
+  check_cuda(cudaStreamWaitEvent(s_in, ev[2 * pieces], 0), "cudaStreamWaitEvent");
   const size_t row_bytes = static_cast<size_t>(n) * d * q.element_size();
   const float scale = 1.0f / std::sqrt(static_cast<float>(d));
   const int dtype = q.scalar_type() == torch::kBFloat16 ? MFA_DTYPE_BF16 : MFA_DTYPE_FP16;
@@ -295,13 +304,13 @@ void flash_attn_forward_pinned(torch::Tensor q, torch::Tensor k, torch::Tensor v
             "copy of k") ||
         !ok(cudaMemcpyAsync(at_row(dv, a), at_row(v, a), bytes, cudaMemcpyHostToDevice, s_in),
             "copy of v") ||
-        !ok(cudaEventRecord(events.ev[2 * i], s_in), "cudaEventRecord") ||
-        !ok(cudaStreamWaitEvent(s_run, events.ev[2 * i], 0), "cudaStreamWaitEvent"))
+        !ok(cudaEventRecord(ev[2 * i], s_in), "cudaEventRecord") ||
+        !ok(cudaStreamWaitEvent(s_run, ev[2 * i], 0), "cudaStreamWaitEvent"))
       break;
     rc = mfa_fwd(at_row(dq, a), at_row(dk, a), at_row(dv, a), at_row(dout, a), 1, b - a, n,
                  static_cast<int32_t>(d), scale, causal ? 1 : 0, dtype, MFA_LAYOUT_BHND,
                  static_cast<void*>(s_run));
-    if (rc != MFA_OK || !ok(cudaEventRecord(events.ev[2 * i + 1], s_run), "cudaEventRecord"))
+    if (rc != MFA_OK || !ok(cudaEventRecord(ev[2 * i + 1], s_run), "cudaEventRecord"))
       break;
     issued = i + 1;
   }
@@ -312,18 +321,21 @@ void flash_attn_forward_pinned(torch::Tensor q, torch::Tensor k, torch::Tensor v
   for (size_t i = 0; i < issued; ++i) {
     const int64_t a = bounds[i], b = bounds[i + 1];
     const size_t bytes = static_cast<size_t>(b - a) * row_bytes;
-    if (!ok(cudaStreamWaitEvent(s_out, events.ev[2 * i + 1], 0), "cudaStreamWaitEvent") ||
+    if (!ok(cudaStreamWaitEvent(s_out, ev[2 * i + 1], 0), "cudaStreamWaitEvent") ||
         (i + 2 == pieces && issued == pieces &&
-         !ok(cudaStreamWaitEvent(s_out, events.ev[2 * (pieces - 1)], 0), "cudaStreamWaitEvent")) ||
+         !ok(cudaStreamWaitEvent(s_out, ev[2 * (pieces - 1)], 0), "cudaStreamWaitEvent")) ||
         !ok(cudaMemcpyAsync(at_row(out, a), at_row(dout, a), bytes, cudaMemcpyDeviceToHost, s_out),
             "copy of the output"))
       break;
   }
   // Every use of the device buffers is on these three streams: once they are drained the
-  // buffers may return to the allocator's current stream.
-  const cudaError_t e_in = cudaStreamSynchronize(s_in);
-  const cudaError_t e_run = cudaStreamSynchronize(s_run);
+  // buffers may return to the allocator's current stream. When every piece was issued, the
+  // last copy out waits for the last forward, which waits for the last copies in, so draining
+  // the copy-out stream drains all three.
+  const bool complete = rc == MFA_OK && err == cudaSuccess && issued == pieces;
   const cudaError_t e_out = cudaStreamSynchronize(s_out);
+  const cudaError_t e_in = complete ? cudaSuccess : cudaStreamSynchronize(s_in);
+  const cudaError_t e_run = complete ? cudaSuccess : cudaStreamSynchronize(s_run);
   if (rc != MFA_OK) throw std::runtime_error(mfa_last_error_string());
   check_cuda(err, what ? what : "");
   check_cuda(e_in, "copies in");
